@@ -1,0 +1,1 @@
+"""CPU parity oracle (test infrastructure only; never imported by the product)."""
