@@ -1,0 +1,432 @@
+"""Benchmark of the B200 block-FP8 linear path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...        (N > 1)
+
+Headline workload (the one defined at 1/2/4/8 GPUs): the
+Qwen3-8B gate_up projection as one blockfp8 linear call -- the activation
+quantizer plus the block-scaled GEMM -- M = 8192, N = 24576, K = 4096, with
+N split into contiguous multiple-of-128 slices, one per GPU, and x
+replicated (each GPU quantizes it itself).  No collective on this path.
+value = 2 M N K per step / (max over ranks of the device time per step),
+in TFLOPS; total work is fixed as N grows ("strong" scaling).
+
+Timing: per-step CUDA events on the launching stream; every timed step is
+preceded by an untimed 512 MiB write that flushes the 126 MB L2, so weights
+and activations come from HBM; W untimed warm-up steps first; a barrier and
+torch.cuda.synchronize() on both sides of the K timed steps; nvidia-smi
+samples the clocks during them.
+
+At N = 1, rank 0 also reports:
+  decode   BASELINE config 2: the four Qwen3-8B shapes x M in {1..32}, linear
+           time and weight GB/s = (N K + 4 nb kb) / t against HBM;
+  prefill  BASELINE config 3: the four shapes x M in {100 .. 8192}, linear
+           and GEMM-only TFLOPS;
+  roofline of the dominant kernel (the GEMM) and cpu_baseline (the CPU
+           oracle on a row sample of the same workload, timed on this host).
+
+--impl reference times the reference's algorithm on the host CPU (the
+oracle port in oracle/: the C quantizer + float64 BLAS GEMM, all host
+threads) on a bounded row sample of the same workload, same metric.
+"""
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "block-FP8 linear TFLOPS (prefill M) & weight GB/s (decode M) per B200, 1/2/4/8 GPU"
+LAYERS = {"qkv": (6144, 4096), "o": (4096, 4096), "gate_up": (24576, 4096), "down": (4096, 12288)}
+HEADLINE = ("gate_up", 8192)
+DECODE_M = [1, 2, 4, 8, 16, 32]
+PREFILL_M = [100, 384, 512, 768, 1024, 2048, 3000, 4096, 8192]
+FLUSH_BYTES = 512 << 20
+REF_SAMPLE_ROWS = 128
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-sweeps", action="store_true", help="skip the decode/prefill sweeps")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--profile-case", default=None,
+                    help="run only LAYER:M a few times (for ncu), e.g. gate_up:8192")
+    return ap.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"],
+                "bf16_tflops_sustained": p["bf16_tflops_sustained"], "source": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+                "source": "fallback"}
+
+
+# ---- data ----------------------------------------------------------------------
+
+def make_weights(n, k, dev, seed=0, rows=None):
+    """w ~ N(0, 0.02) from a CPU generator (fixed seed), quantized in 128 x 128
+    blocks; rows=(lo, hi) keeps a slice (multiples of 128 keep blocks whole)."""
+    import blockfp8_b200 as bf
+    g = torch.Generator().manual_seed(seed)
+    w = torch.randn(n, k, generator=g) * 0.02
+    if rows is not None:
+        w = w[rows[0]:rows[1]]
+    return bf.quantize_weights(w.to(dev))
+
+
+def make_x(m, k, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(m, k, generator=g).to(torch.bfloat16)
+
+
+# ---- timing helpers ------------------------------------------------------------
+
+class Flusher:
+    def __init__(self, dev):
+        self.buf = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+
+    def __call__(self):
+        self.buf.fill_(1.0)
+
+
+def time_device(fn, reps, flush, warmup=3):
+    """Median and mean device microseconds of fn() over reps, L2 flushed before each."""
+    for _ in range(warmup):
+        fn()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
+    for i in range(reps):
+        flush()
+        starts[i].record()
+        fn()
+        ends[i].record()
+    torch.cuda.synchronize()
+    us = [s.elapsed_time(e) * 1e3 for s, e in zip(starts, ends)]
+    return statistics.median(us), statistics.fmean(us)
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples of this GPU during a timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, dev):
+        self.proc = None
+        try:
+            uuid = str(torch.cuda.get_device_properties(dev).uuid)
+            uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", uuid, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"available": False}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out = ""
+        rows = [r.split(",") for r in out.strip().splitlines() if r.count(",") >= 7]
+        if not rows:
+            return {"available": False}
+        sm = [float(r[0]) for r in rows]
+        mx = max(float(r[1]) for r in rows)
+        power = [float(r[2]) for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[4 + i]})
+        loaded = [s for s, p in zip(sm, power) if p > 0.5 * max(power)] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(power)}
+
+
+# ---- distributed plumbing --------------------------------------------------------
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                timeout=datetime.timedelta(seconds=300))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---- the CPU legs (oracle; test infrastructure, only timed here) ------------------
+
+def cpu_sample(rows: int, seed: int = 0):
+    """A row sample of the headline workload, prepared for the CPU oracle."""
+    from oracle import oracle as O
+    name, m = HEADLINE
+    n, k = LAYERS[name]
+    x = make_x(m, k, seed)[:rows]
+    w = torch.randn(n, k, generator=torch.Generator().manual_seed(seed)) * 0.02
+    b, sb = O.quantize_weights(w.numpy())
+    xbits = x.view(torch.int16).numpy().view(np.uint16)
+    return O, xbits, b, sb, n, k
+
+
+def cpu_step(O, xbits, b, sb):
+    a, sa = O.quantize_activations(xbits)
+    return O.reference_gemm(a, sa, b, sb)
+
+
+def cpu_threads():
+    return int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+
+
+def run_cpu_baseline(rows=REF_SAMPLE_ROWS, reps=2):
+    O, xbits, b, sb, n, k = cpu_sample(rows)
+    cpu_step(O, xbits, b, sb)  # warm (BLAS threads, page faults)
+    t = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        cpu_step(O, xbits, b, sb)
+        t.append(time.perf_counter() - t0)
+    sec = statistics.median(t)
+    return {"value": 2 * rows * n * k / sec / 1e12, "unit": "TFLOPS", "cores": cpu_threads(),
+            "kind": "port",
+            "sample": f"{rows} of the 8192 activation rows of gate_up (N=24576, K=4096): oracle "
+                      f"quantize_activations (C, OpenMP) + reference_gemm (float64 BLAS), "
+                      f"median of {reps}, {sec:.2f} s per sample"}
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    O, xbits, b, sb, n, k = cpu_sample(REF_SAMPLE_ROWS)
+    for _ in range(max(1, args.warmup)):
+        cpu_step(O, xbits, b, sb)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_step(O, xbits, b, sb)
+    sec = (time.perf_counter() - t0) / args.steps
+    value = 2 * REF_SAMPLE_ROWS * n * k / sec / 1e12
+    name, m = HEADLINE
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOPS",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f64 (the reference's CPU oracle)", "data": "synthetic (seeded N(0,1) x, N(0,0.02) w)",
+        "config": {"workload": f"{name} linear M={m} N={n} K={k}, a row sample per step", "M": m,
+                   "N": n, "K": k, "sample_rows": REF_SAMPLE_ROWS},
+        "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": cpu_threads(), "kind": "port",
+                         "sample": f"{REF_SAMPLE_ROWS} of {m} rows per step"},
+        "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---- GPU legs -----------------------------------------------------------------------
+
+def fp8_gemm_flops(m, n, k):
+    return 2.0 * m * n * k
+
+
+def weight_bytes(n, k):
+    return n * k + 4 * (-(-n // 128)) * (-(-k // 128))
+
+
+def sweeps(dev, flush, reps=20):
+    import blockfp8_b200 as bf
+    out = {"decode": {}, "prefill": {}}
+    for name, (n, k) in LAYERS.items():
+        b, sb = make_weights(n, k, dev, seed=1)
+        for m in DECODE_M:
+            x = make_x(m, k, seed=m).to(dev)
+            med, _ = time_device(lambda: bf.linear(x, b, sb), reps, flush)
+            gbs = weight_bytes(n, k) / (med * 1e-6) / 1e9
+            out["decode"][f"{name}_m{m}"] = {"us": round(med, 2), "weight_gbs": round(gbs, 1)}
+        for m in PREFILL_M:
+            x = make_x(m, k, seed=m).to(dev)
+            q, s = bf.quantize_cuda(x)
+            med, _ = time_device(lambda: bf.linear(x, b, sb), max(5, reps // 2), flush)
+            gmed, _ = time_device(lambda: bf.gemm(q, s, b, sb), max(5, reps // 2), flush)
+            f = fp8_gemm_flops(m, n, k)
+            out["prefill"][f"{name}_m{m}"] = {"linear_us": round(med, 1), "gemm_us": round(gmed, 1),
+                                              "linear_tflops": round(f / (med * 1e-6) / 1e12, 1),
+                                              "gemm_tflops": round(f / (gmed * 1e-6) / 1e12, 1)}
+        del b, sb
+        torch.cuda.empty_cache()
+    return out
+
+
+def profile_case(spec):
+    """A few launches of one case, for ncu (no timing printed)."""
+    import blockfp8_b200 as bf
+    name, m = spec.split(":")
+    m = int(m)
+    n, k = LAYERS[name]
+    dev = torch.device("cuda", 0)
+    b, sb = make_weights(n, k, dev, seed=1)
+    x = make_x(m, k).to(dev)
+    for _ in range(3):
+        bf.linear(x, b, sb)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": spec, "ok": True}))
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    if args.profile_case:
+        return profile_case(args.profile_case)
+    world, rank, local = dist_setup(args)
+    dev = torch.device("cuda", local)
+    import blockfp8_b200 as bf
+    if not bf.native_available():
+        raise RuntimeError("native libraries missing: run python -m blockfp8_b200.build")
+
+    name, m = HEADLINE
+    n, k = LAYERS[name]
+    assert n % (128 * world) == 0, "N must split into multiple-of-128 slices"
+    n_per = n // world
+    b, sb = make_weights(n, k, dev, seed=0, rows=(rank * n_per, (rank + 1) * n_per))
+    x_cpu = make_x(m, k, seed=0)
+    x = x_cpu.to(dev)
+    flush = Flusher(dev)
+    flops_total = fp8_gemm_flops(m, n, k)
+
+    # warm-up (untimed)
+    for _ in range(args.warmup):
+        flush()
+        bf.linear(x, b, sb)
+    torch.cuda.synchronize()
+
+    # ---- the timed K steps: blockfp8.linear, L2 flushed before each
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    clocks = ClockSampler(dev) if rank == 0 else None
+    time.sleep(0.3 if clocks else 0)
+    barrier(world)
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        flush()
+        starts[i].record()
+        y = bf.linear(x, b, sb)
+        ends[i].record()
+    torch.cuda.synchronize()
+    barrier(world)
+    clock_info = clocks.stop() if clocks else None
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    mine = statistics.fmean(step_ms)
+    ms = max_over_ranks(mine, world)
+    value = flops_total / (ms * 1e-3) / 1e12
+
+    # ---- kernel breakdown inside the same flushed protocol: quantizer, GEMM
+    q, s = bf.quantize_cuda(x)
+    quant_us, _ = time_device(lambda: bf.quantize_cuda(x), args.steps, flush)
+    gemm_med, gemm_us = time_device(lambda: bf.gemm(q, s, b, sb), args.steps, flush)
+    gemm_tflops = fp8_gemm_flops(m, n_per, k) / (gemm_us * 1e-6) / 1e12
+    pk = peaks()
+    fp8_peak = 2.0 * pk["bf16_tflops"]
+
+    # ---- e2e: host (pinned) activations in, host output back, through linear
+    x_host = x_cpu.pin_memory()
+    y_host = torch.empty(m, n_per, dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        xd = x_host.to(dev, non_blocking=True)
+        yd = bf.linear(xd, b, sb)
+        y_host.copy_(yd, non_blocking=True)
+
+    e2e_med, e2e_mean = time_device(e2e_step, max(3, args.steps // 2), flush)
+    e2e_ms = max_over_ranks(e2e_mean / 1e3, world)
+
+    line = None
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "TFLOPS", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "e4m3 x e4m3 -> f32 (bf16 in/out)",
+            "data": "synthetic: seeded CPU N(0,1) bf16 activations, N(0,0.02) weights quantized in "
+                    "128x128 blocks",
+            "config": {"workload": f"{name} linear (quantize + GEMM) M={m} N={n} K={k}, N "
+                                   f"column-sharded into {world} slice(s) of {n_per}",
+                       "M": m, "N": n, "K": k, "n_per_gpu": n_per,
+                       "parallelism": f"column-parallel N/{world}, x replicated, no collective",
+                       "l2": "flushed by a 512 MiB write before every timed step"},
+            "roofline": {"bound": "tensor", "kernel": "gemm_kernel (tcgen05 e4m3)",
+                         "achieved": round(gemm_tflops, 1), "peak": round(fp8_peak, 1),
+                         "unit": "TFLOP/s", "frac": round(gemm_tflops / fp8_peak, 4),
+                         "peak_source": f"2 x bf16_tflops of MEASURED_PEAKS.json ({pk['source']}): "
+                                        "dense e4m3 runs at twice the bf16 rate",
+                         "traffic": None,
+                         "algorithmic": f"2*M*N*K = {fp8_gemm_flops(m, n_per, k):.4g} FLOP per launch"},
+            "breakdown_us": {"quantize": round(quant_us, 2), "gemm_mean": round(gemm_us, 2),
+                             "gemm_median": round(gemm_med, 2), "linear_mean": round(mine * 1e3, 2)},
+            "e2e": {"value": round(flops_total / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOPS",
+                    "h2d_bytes_per_step": m * k * 2, "d2h_bytes_per_step": m * n_per * 2,
+                    "ms_per_step": round(e2e_ms, 3)},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clock_info,
+        }
+    if world == 1:
+        if not args.no_sweeps:
+            line["sweeps"] = sweeps(dev, flush)
+            dec = line["sweeps"]["decode"]
+            best = {k_: v for k_, v in dec.items() if int(k_.split("_m")[1]) <= 16}
+            line["decode_roofline"] = {
+                "bound": "hbm", "unit": "GB/s", "peak": pk["hbm_gbs"],
+                "peak_source": f"hbm_gbs of MEASURED_PEAKS.json ({pk['source']}, a copy figure)",
+                "min_frac_m_le_16": round(min(v["weight_gbs"] for v in best.values()) / pk["hbm_gbs"], 3),
+                "median_frac_m_le_16": round(statistics.median(v["weight_gbs"] for v in best.values())
+                                             / pk["hbm_gbs"], 3)}
+        if not args.no_cpu:
+            line["cpu_baseline"] = run_cpu_baseline()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,145 @@
+"""Loading the native libraries: the C ABI (ctypes) and the torch op library.
+
+libblockfp8_b200.so carries the kernels behind the C ABI declared in
+include/blockfp8_b200.h; _C.so registers torch.ops.blockfp8.* on top of it.
+Both are built in-tree by blockfp8_b200/build.py.  Nothing here falls back
+to another implementation: when a library is missing, the functions that
+need it raise.
+"""
+
+import ctypes
+import os
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CAPI_LIB = os.path.join(HERE, "libblockfp8_b200.so")
+OPS_LIB = os.path.join(HERE, "_C.so")
+
+BFP8_OK = 0
+BFP8_EINVAL = -1
+BFP8_ECUDA = -2
+
+
+class GemmProblem(ctypes.Structure):
+    """bfp8_gemm_problem (include/blockfp8_b200.h)."""
+    _fields_ = [
+        ("a", ctypes.c_void_p), ("lda", ctypes.c_int64),
+        ("b", ctypes.c_void_p), ("ldb", ctypes.c_int64),
+        ("sa", ctypes.c_void_p), ("sa_m", ctypes.c_int64), ("sa_k", ctypes.c_int64),
+        ("sb", ctypes.c_void_p), ("sb_n", ctypes.c_int64), ("sb_k", ctypes.c_int64),
+        ("c", ctypes.c_void_p), ("ldc", ctypes.c_int64),
+        ("M", ctypes.c_int), ("N", ctypes.c_int), ("K", ctypes.c_int),
+        ("eps", ctypes.c_float),
+    ]
+
+
+class Plan(ctypes.Structure):
+    """bfp8_plan."""
+    _fields_ = [("config", ctypes.c_int), ("splits", ctypes.c_int), ("fused", ctypes.c_int)]
+
+    def __repr__(self):
+        return f"Plan(config={self.config}, splits={self.splits}, fused={self.fused})"
+
+
+class QuantProblem(ctypes.Structure):
+    """bfp8_quant_problem."""
+    _fields_ = [
+        ("x", ctypes.c_void_p), ("ldx", ctypes.c_int64),
+        ("q", ctypes.c_void_p), ("ldq", ctypes.c_int64),
+        ("s", ctypes.c_void_p), ("s_m", ctypes.c_int64), ("s_k", ctypes.c_int64),
+        ("M", ctypes.c_int), ("K", ctypes.c_int), ("eps", ctypes.c_float),
+    ]
+
+
+# Every function the header declares, with its ctypes signature.
+_SIGNATURES = {
+    "bfp8_abi_version": ([], ctypes.c_int),
+    "bfp8_last_error": ([], ctypes.c_char_p),
+    "bfp8_num_configs": ([], ctypes.c_int),
+    "bfp8_config_name": ([ctypes.c_int], ctypes.c_char_p),
+    "bfp8_num_fused_configs": ([], ctypes.c_int),
+    "bfp8_fused_config_name": ([ctypes.c_int], ctypes.c_char_p),
+    "bfp8_choose_plan": ([ctypes.c_int] * 4, Plan),
+    "bfp8_choose_fused_plan": ([ctypes.c_int] * 4, Plan),
+    "bfp8_prefers_fused": ([ctypes.c_int] * 3, ctypes.c_int),
+    "bfp8_plan_shape": ([ctypes.POINTER(GemmProblem), Plan, ctypes.POINTER(ctypes.c_int),
+                         ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
+    "bfp8_workspace_bytes": ([ctypes.POINTER(GemmProblem), Plan], ctypes.c_int64),
+    "bfp8_counters_needed": ([ctypes.POINTER(GemmProblem), Plan], ctypes.c_int),
+    "bfp8_launch_gemm": ([ctypes.POINTER(GemmProblem), Plan, ctypes.c_void_p, ctypes.c_void_p,
+                          ctypes.c_void_p], ctypes.c_int),
+    "bfp8_launch_quantize": ([ctypes.POINTER(QuantProblem), ctypes.c_void_p], ctypes.c_int),
+    "bfp8_device_status": ([ctypes.c_int], ctypes.c_int64),
+}
+
+_capi = None
+_ops_loaded = False
+
+
+def capi() -> ctypes.CDLL:
+    """The C ABI library; raises if it has not been built."""
+    global _capi
+    if _capi is None:
+        if not os.path.exists(CAPI_LIB):
+            raise RuntimeError(f"native library not built ({CAPI_LIB} missing); "
+                               "run python -m blockfp8_b200.build")
+        lib = ctypes.CDLL(CAPI_LIB)
+        for name, (args, res) in _SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.argtypes = args
+            fn.restype = res
+        _capi = lib
+    return _capi
+
+
+def capi_loaded() -> bool:
+    return _capi is not None
+
+
+def check(status: int) -> None:
+    """Raise RuntimeError with the library's message for a failed call."""
+    if status < 0:
+        raise RuntimeError(capi().bfp8_last_error().decode())
+
+
+def load_ops() -> bool:
+    """Load _C.so (torch.ops.blockfp8.*) and register the fake kernels once."""
+    global _ops_loaded
+    if not _ops_loaded and os.path.exists(OPS_LIB):
+        capi()  # the same library _C.so links against, loaded first by path
+        torch.ops.load_library(OPS_LIB)
+        _register_fakes()
+        _ops_loaded = True
+    return _ops_loaded
+
+
+def _register_fakes() -> None:
+    """Shape functions so torch.compile (and vLLM) can trace through the ops
+    (the reference's blockfp8/gemm.py:23-43)."""
+
+    @torch.library.register_fake("blockfp8::gemm")
+    def _(a, a_scales, b, b_scales, config=-1, split_k=0):
+        return a.new_empty((a.shape[0], b.shape[0]), dtype=torch.bfloat16)
+
+    @torch.library.register_fake("blockfp8::gemm_bf16")
+    def _(x, b, b_scales, config=-1, split_k=0, eps=1e-10):
+        return x.new_empty((x.shape[0], b.shape[0]), dtype=torch.bfloat16)
+
+    @torch.library.register_fake("blockfp8::linear")
+    def _(x, b, b_scales):
+        return x.new_empty((x.shape[0], b.shape[0]), dtype=torch.bfloat16)
+
+    @torch.library.register_fake("blockfp8::quantize")
+    def _(x, eps=1e-10):
+        m, k = x.shape
+        q = x.new_empty((m, k), dtype=torch.float8_e4m3fn)
+        s = x.new_empty(((k + 127) // 128, m), dtype=torch.float32).t()
+        return q, s
+
+
+def device_status(reset: bool = False) -> int:
+    """Watchdog word of the current device (0 = no kernel gave up a wait)."""
+    v = capi().bfp8_device_status(1 if reset else 0)
+    check(v if v < 0 else 0)
+    return v

@@ -1,0 +1,478 @@
+// Host side of blockfp8_b200: configurations, the planner, tensor maps,
+// launches and the C ABI declared in include/blockfp8_b200.h.
+//
+// Counterparts in the reference (simon-jd/blockfp8): csrc/gemm_sm89.cu
+// (configurations :71-114, plan lookup :159-224, split sizing :250-279,
+// launch :281-286) and csrc/quant_sm89.cu:66-71.  The tables, the cost model
+// and the launch plumbing here are written for B200: 148 SMs, one
+// persistent CTA per SM, tensor maps for TMA.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "blockfp8_b200.h"
+
+#include "gemm_kernel.cuh"
+#include "quantize.cuh"
+
+namespace bfp8 {
+namespace {
+
+thread_local std::string t_last_error;
+
+int fail(int code, const std::string& msg) {
+  t_last_error = "blockfp8: " + msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  cudaGetLastError();  // not sticky: do not leave it for the caller's next check
+  return fail(BFP8_ECUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+int cdiv(int a, int b) { return (a + b - 1) / b; }
+
+// ---- compiled configurations ---------------------------------------------------
+
+struct ConfigEntry {
+  const char* name;
+  int bn, stages, threads, smem;
+  const void* kernel;
+  void (*launch)(const GemmParams&, int grid, cudaStream_t);
+};
+
+template <class Cfg>
+void launch_cfg(const GemmParams& gp, int grid, cudaStream_t stream) {
+  gemm_kernel<Cfg><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(gp);
+}
+
+template <class Cfg>
+ConfigEntry entry(const char* name) {
+  return {name, Cfg::BN, Cfg::STAGES, Cfg::THREADS, Cfg::SMEM_BYTES,
+          reinterpret_cast<const void*>(&gemm_kernel<Cfg>), &launch_cfg<Cfg>};
+}
+
+//                        BN  stages
+using Cfg256 = GemmCfg<256, 4>;
+using Cfg128 = GemmCfg<128, 6>;
+using Cfg64 = GemmCfg<64, 8>;
+
+const ConfigEntry kConfigs[] = {
+    entry<Cfg256>("m128n256s4"),
+    entry<Cfg128>("m128n128s6"),
+    entry<Cfg64>("m128n64s8"),
+};
+constexpr int kNumConfigs = int(sizeof(kConfigs) / sizeof(kConfigs[0]));
+// The fused path (gemm_bf16) quantizes into the workspace, then runs the
+// same GEMM kernels, so it has the same configurations.
+constexpr int kNumFusedConfigs = kNumConfigs;
+
+bool config_ok(int config) { return config >= 0 && config < kNumConfigs; }
+
+// ---- per-device state -------------------------------------------------------------
+
+constexpr int kMaxDevices = 64;
+
+int current_device_sms(int* dev_out) {
+  static std::atomic<int> sms[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  if (dev_out) *dev_out = dev;
+  if (dev >= kMaxDevices) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n;
+  }
+  int n = sms[dev].load(std::memory_order_relaxed);
+  if (n == 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
+    sms[dev].store(n, std::memory_order_relaxed);
+  }
+  return n;
+}
+
+// The dynamic shared-memory limit is a per-device attribute of a kernel:
+// set it on the first launch of each configuration on each device.
+int ensure_smem_attr(int config, int dev) {
+  static std::atomic<uint64_t> done[kNumConfigs] = {};
+  const uint64_t bit = dev < 64 ? (uint64_t(1) << dev) : 0;
+  if (bit && (done[config].load(std::memory_order_acquire) & bit)) return BFP8_OK;
+  const ConfigEntry& e = kConfigs[config];
+  cudaError_t err = cudaFuncSetAttribute(e.kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, e.smem);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaFuncSetAttribute(MaxDynamicSharedMemorySize)");
+  done[config].fetch_or(bit, std::memory_order_release);
+  return BFP8_OK;
+}
+
+// ---- tensor maps --------------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+int make_map(CUtensorMap* map, CUtensorMapDataType dtype, const void* ptr, uint64_t inner,
+             uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer) {
+  auto fn = encode_fn();
+  if (!fn) return fail(BFP8_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estrides[2] = {1, 1};
+  CUresult r = fn(map, dtype, 2, const_cast<void*>(ptr), dims, strides, box, estrides,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(BFP8_ECUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
+  return BFP8_OK;
+}
+
+// ---- plan tables (B200) ----------------------------------------------------------
+
+struct TableEntry {
+  int n, k, m, config, splits;
+};
+// Winners of the autotuning sweep on a B200 (blockfp8_b200/autotune.py).
+const TableEntry kPlanTable[] = {
+#include "plan_table.inc"
+    {0, 0, 0, 0, 0}};
+constexpr int kPlanEntries = int(sizeof(kPlanTable) / sizeof(kPlanTable[0])) - 1;
+
+// Fused-path winners and whether each beat quantize-then-GEMM.
+struct FusedEntry {
+  int n, k, m, config, splits, wins;
+};
+const FusedEntry kFusedTable[] = {
+#include "fused_plan_table.inc"
+    {0, 0, 0, 0, 0, 0}};
+constexpr int kFusedEntries = int(sizeof(kFusedTable) / sizeof(kFusedTable[0])) - 1;
+
+// The entry for this (N, K) with the smallest tabulated M >= M, else the
+// largest (the reference's lookup rule, csrc/gemm_sm89.cu:158-169).
+template <class E>
+const E* lookup(const E* table, int n_entries, int M, int N, int K) {
+  const E* best = nullptr;
+  for (int i = 0; i < n_entries; ++i) {
+    const E& t = table[i];
+    if (t.n != N || t.k != K || !config_ok(t.config)) continue;
+    const bool better =
+        !best || (t.m >= M ? (best->m < M || t.m < best->m) : (best->m < M && t.m > best->m));
+    if (better) best = &t;
+  }
+  return best;
+}
+
+// Cost model of one plan on B200, in nanoseconds, for untabulated shapes and
+// for the balanced choice between tabulated plans.  A persistent CTA per SM
+// runs ceil(units / SMs) units of k_per_split K blocks; a K block costs the
+// larger of its MMA time (4 MMAs of 128 x BN x 32 at 8192 e4m3 MACs per SM
+// clock) and its operand bytes at the SM's share of HBM bandwidth; split-K
+// adds the fp32 partial round trip of the valid rows.
+double plan_cost_ns(int M, int N, int K, int num_sms, int config, int splits) {
+  const ConfigEntry& e = kConfigs[config];
+  const int k_tiles = cdiv(K, 128);
+  const int per = cdiv(k_tiles, std::max(1, std::min(splits, k_tiles)));
+  const int real_splits = cdiv(k_tiles, per);
+  const int tiles_m = cdiv(M, 128), tiles_n = cdiv(N, e.bn);
+  const int64_t units = int64_t(tiles_m) * tiles_n * real_splits;
+  const int64_t waves = (units + num_sms - 1) / num_sms;
+  const int active = int(std::min<int64_t>(units, num_sms));
+  const double clk_ghz = 1.8;
+  const double mma_ns = 2.0 * e.bn / clk_ghz;
+  const int rows = std::min(M, 128);
+  const double bytes = double(rows) * 128 + double(std::min(N, e.bn)) * 128;
+  const double hbm_gbs = 6500.0, l2_sm_gbs = 120.0;
+  const double sm_gbs = std::min(l2_sm_gbs, hbm_gbs / active);
+  const double load_ns = bytes / sm_gbs;
+  double t = double(waves) * per * std::max(mma_ns, load_ns);
+  const double tile_out = double(rows) * e.bn;
+  t += double(waves) * tile_out * 2 / (hbm_gbs / active) * 1.0;  // bf16 store
+  if (real_splits > 1) t += double(waves) * tile_out * 4 * 2 / sm_gbs + 600.0;
+  return t + 2000.0;  // launch and pipeline fill
+}
+
+bfp8_plan heuristic_plan(int M, int N, int K, int num_sms, bool fused) {
+  bfp8_plan best{1, 1, fused ? 1 : 0};
+  double best_t = 1e300;
+  const int k_tiles = cdiv(K, 128);
+  for (int config = 0; config < kNumConfigs; ++config) {
+    for (int splits = 1; splits <= std::min(k_tiles, 16); ++splits) {
+      const int per = cdiv(k_tiles, splits);
+      if (cdiv(k_tiles, per) != splits) continue;  // same as a smaller split count
+      const double t = plan_cost_ns(M, N, K, num_sms, config, splits);
+      if (t < best_t * 0.999) {
+        best_t = t;
+        best = {config, splits, fused ? 1 : 0};
+      }
+    }
+  }
+  return best;
+}
+
+// Among the plans tabulated for this shape at M / 4 .. 4 M, the one the cost
+// model rates fastest at this M; ties keep the entry above (the reference's
+// balanced_entry, csrc/gemm_sm89.cu:190-224, with the B200 cost model in place
+// of its busiest-SM work count).
+const TableEntry* balanced_entry(const TableEntry* above, int M, int N, int K, int num_sms) {
+  if (M < 256 || above->m == M) return above;
+  const TableEntry* best = above;
+  double best_t = plan_cost_ns(M, N, K, num_sms, above->config, above->splits);
+  for (int i = 0; i < kPlanEntries; ++i) {
+    const TableEntry& t = kPlanTable[i];
+    if (t.n != N || t.k != K || !config_ok(t.config)) continue;
+    if (4 * int64_t(t.m) < M || t.m > 4 * int64_t(M)) continue;
+    const double c = plan_cost_ns(M, N, K, num_sms, t.config, t.splits);
+    if (c < best_t * 0.98) {
+      best = &t;
+      best_t = c;
+    }
+  }
+  return best;
+}
+
+struct Derived {
+  int tiles_m, tiles_n, tiles, k_tiles, k_per_split, splits;
+};
+
+Derived derive(const bfp8_gemm_problem& p, const bfp8_plan& plan) {
+  const ConfigEntry& e = kConfigs[plan.config];
+  Derived d;
+  d.tiles_m = cdiv(p.M, 128);
+  d.tiles_n = cdiv(p.N, e.bn);
+  d.tiles = d.tiles_m * d.tiles_n;
+  d.k_tiles = cdiv(p.K, 128);
+  const int splits = std::max(1, std::min(plan.splits, d.k_tiles));
+  d.k_per_split = cdiv(d.k_tiles, splits);
+  d.splits = cdiv(d.k_tiles, d.k_per_split);  // no empty splits
+  return d;
+}
+
+int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
+
+// Fused plans: quantized activations [M, K] then M-major scales [kb, M].
+int64_t fused_front_bytes(const bfp8_gemm_problem& p) {
+  const int64_t kb = cdiv(p.K, 128);
+  return align256(int64_t(p.M) * p.K) + align256(kb * p.M * 4);
+}
+
+int64_t splitk_bytes(const bfp8_gemm_problem& p, const bfp8_plan& plan) {
+  const Derived d = derive(p, plan);
+  if (d.splits == 1) return 0;
+  return int64_t(d.splits) * d.tiles * 128 * kConfigs[plan.config].bn * int64_t(sizeof(float));
+}
+
+bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+int check_problem(const bfp8_gemm_problem& p, bool fused) {
+  if (p.M < 0 || p.N <= 0 || p.K <= 0) return fail(BFP8_EINVAL, "bad shapes (M >= 0, N > 0, K > 0)");
+  if (p.K % 16 != 0) return fail(BFP8_EINVAL, "K must be a positive multiple of 16");
+  if (p.N % 8 != 0) return fail(BFP8_EINVAL, "N must be a positive multiple of 8");
+  if (p.M == 0) return BFP8_OK;
+  if (!p.a || !p.b || !p.c || !p.sb || (!fused && !p.sa)) return fail(BFP8_EINVAL, "null operand pointer");
+  if (!aligned16(p.a) || !aligned16(p.b) || !aligned16(p.c))
+    return fail(BFP8_EINVAL, "a, b and c must be 16-byte aligned");
+  const int64_t a_elem = fused ? 2 : 1;
+  if (p.lda < p.K || (p.lda * a_elem) % 16 != 0)
+    return fail(BFP8_EINVAL, "a must be row-major with 16-byte aligned rows");
+  if (p.ldb < p.K || p.ldb % 16 != 0) return fail(BFP8_EINVAL, "b must be row-major with 16-element aligned rows");
+  if (p.ldc < p.N || p.ldc % 8 != 0) return fail(BFP8_EINVAL, "c must be row-major with 8-element aligned rows");
+  if (fused && !(p.eps > 0.f)) return fail(BFP8_EINVAL, "eps must be positive");
+  return BFP8_OK;
+}
+
+int launch_quant(const QuantParams& qp, cudaStream_t stream, int num_sms) {
+  const int64_t groups = int64_t(qp.M) * qp.kb;
+  if (groups == 0) return BFP8_OK;
+  const int64_t per_cta = kQuantThreads / 16;
+  const int64_t want = (groups + per_cta - 1) / per_cta;
+  const int grid = int(std::min<int64_t>(want, int64_t(num_sms) * 8));
+  quantize_kernel<<<grid, kQuantThreads, 0, stream>>>(qp);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "quantize kernel launch");
+  return BFP8_OK;
+}
+
+}  // namespace
+}  // namespace bfp8
+
+using namespace bfp8;
+
+extern "C" {
+
+int bfp8_abi_version(void) { return 1; }
+
+const char* bfp8_last_error(void) { return t_last_error.c_str(); }
+
+int bfp8_num_configs(void) { return kNumConfigs; }
+int bfp8_num_fused_configs(void) { return kNumFusedConfigs; }
+
+const char* bfp8_config_name(int config) { return config_ok(config) ? kConfigs[config].name : nullptr; }
+const char* bfp8_fused_config_name(int config) {
+  return config_ok(config) ? kConfigs[config].name : nullptr;
+}
+
+bfp8_plan bfp8_choose_plan(int M, int N, int K, int num_sms) {
+  if (const TableEntry* t = lookup(kPlanTable, kPlanEntries, M, N, K)) {
+    t = balanced_entry(t, M, N, K, num_sms);
+    return {t->config, t->splits, 0};
+  }
+  return heuristic_plan(M, N, K, num_sms, false);
+}
+
+bfp8_plan bfp8_choose_fused_plan(int M, int N, int K, int num_sms) {
+  if (const FusedEntry* t = lookup(kFusedTable, kFusedEntries, M, N, K))
+    if (M <= t->m) return {t->config, t->splits, 1};
+  return heuristic_plan(M, N, K, num_sms, true);
+}
+
+int bfp8_prefers_fused(int M, int N, int K) {
+  const FusedEntry* t = lookup(kFusedTable, kFusedEntries, M, N, K);
+  return t && M <= t->m && t->wins ? 1 : 0;
+}
+
+int bfp8_plan_shape(const bfp8_gemm_problem* p, bfp8_plan plan, int* tiles, int* k_tiles) {
+  if (!p || !config_ok(plan.config)) return fail(BFP8_EINVAL, "bad config id");
+  const Derived d = derive(*p, plan);
+  if (tiles) *tiles = d.tiles;
+  if (k_tiles) *k_tiles = d.k_tiles;
+  return BFP8_OK;
+}
+
+int64_t bfp8_workspace_bytes(const bfp8_gemm_problem* p, bfp8_plan plan) {
+  if (!p || !config_ok(plan.config)) return fail(BFP8_EINVAL, "bad config id");
+  if (p->M <= 0) return 0;
+  return (plan.fused ? fused_front_bytes(*p) : 0) + splitk_bytes(*p, plan);
+}
+
+int bfp8_counters_needed(const bfp8_gemm_problem* p, bfp8_plan plan) {
+  if (!p || !config_ok(plan.config)) return fail(BFP8_EINVAL, "bad config id");
+  if (p->M <= 0) return 0;
+  const Derived d = derive(*p, plan);
+  return d.splits == 1 ? 0 : d.tiles;
+}
+
+int bfp8_launch_quantize(const bfp8_quant_problem* qp, void* stream) {
+  if (!qp) return fail(BFP8_EINVAL, "null problem");
+  const bfp8_quant_problem& p = *qp;
+  if (p.M < 0 || p.K <= 0 || p.K % 8 != 0) return fail(BFP8_EINVAL, "K must be a positive multiple of 8");
+  if (p.M == 0) return BFP8_OK;
+  if (!p.x || !p.q || !p.s) return fail(BFP8_EINVAL, "null operand pointer");
+  if (!aligned16(p.x) || p.ldx < p.K || p.ldx % 8 != 0)
+    return fail(BFP8_EINVAL, "x must be row-major with 16-byte aligned rows");
+  if ((reinterpret_cast<uintptr_t>(p.q) & 7u) || p.ldq < p.K || p.ldq % 8 != 0)
+    return fail(BFP8_EINVAL, "q must be row-major with 8-byte aligned rows");
+  if (!(p.eps > 0.f)) return fail(BFP8_EINVAL, "eps must be positive");
+  const int sms = current_device_sms(nullptr);
+  if (sms <= 0) return cuda_fail(cudaGetLastError(), "cudaGetDevice");
+  QuantParams q{static_cast<const __nv_bfloat16*>(p.x), p.ldx, static_cast<uint8_t*>(p.q), p.ldq,
+                p.s, p.s_m, p.s_k, p.M, p.K, cdiv(p.K, 128), p.eps};
+  return launch_quant(q, static_cast<cudaStream_t>(stream), sms);
+}
+
+int bfp8_launch_gemm(const bfp8_gemm_problem* pp, bfp8_plan plan, float* workspace, int* counters,
+                     void* stream_) {
+  if (!pp) return fail(BFP8_EINVAL, "null problem");
+  if (!config_ok(plan.config)) return fail(BFP8_EINVAL, "config out of range");
+  if (plan.splits < 1) return fail(BFP8_EINVAL, "splits must be >= 1");
+  bfp8_gemm_problem p = *pp;
+  const bool fused = plan.fused != 0;
+  if (int r = check_problem(p, fused)) return r;
+  if (p.M == 0) return BFP8_OK;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  int dev = 0;
+  const int sms = current_device_sms(&dev);
+  if (sms <= 0) return cuda_fail(cudaGetLastError(), "cudaGetDevice");
+
+  const Derived d = derive(p, plan);
+  if ((fused || d.splits > 1) && !workspace) return fail(BFP8_EINVAL, "workspace required");
+  if (d.splits > 1 && !counters) return fail(BFP8_EINVAL, "split-K counters required");
+
+  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+  if (fused) {
+    // gemm_bf16: quantize x into the front of the workspace (M-major
+    // scales), then the GEMM reads it like any quantized input.
+    uint8_t* q = ws;
+    float* s = reinterpret_cast<float*>(ws + align256(int64_t(p.M) * p.K));
+    QuantParams qp{static_cast<const __nv_bfloat16*>(p.a), p.lda, q, p.K, s, 1, p.M, p.M, p.K,
+                   cdiv(p.K, 128), p.eps};
+    if (int r = launch_quant(qp, stream, sms)) return r;
+    p.a = q;
+    p.lda = p.K;
+    p.sa = s;
+    p.sa_m = 1;
+    p.sa_k = p.M;
+    ws += fused_front_bytes(*pp);
+  }
+
+  const ConfigEntry& e = kConfigs[plan.config];
+  GemmParams gp;
+  std::memset(&gp, 0, sizeof(gp));
+  if (int r = make_map(&gp.map_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.a, uint64_t(p.K), uint64_t(p.M),
+                       uint64_t(p.lda), 128, 128))
+    return r;
+  if (int r = make_map(&gp.map_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.b, uint64_t(p.K), uint64_t(p.N),
+                       uint64_t(p.ldb), 128, uint32_t(e.bn)))
+    return r;
+  if (int r = make_map(&gp.map_c, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.c, uint64_t(p.N),
+                       uint64_t(p.M), uint64_t(p.ldc) * 2, 64, 32))
+    return r;
+  gp.sa = p.sa;
+  gp.sa_m = p.sa_m;
+  gp.sa_k = p.sa_k;
+  gp.sb = p.sb;
+  gp.sb_n = p.sb_n;
+  gp.sb_k = p.sb_k;
+  gp.workspace = reinterpret_cast<float*>(ws);
+  gp.counters = counters;
+  gp.M = p.M;
+  gp.N = p.N;
+  gp.K = p.K;
+  gp.tiles_m = d.tiles_m;
+  gp.tiles_n = d.tiles_n;
+  gp.tiles = d.tiles;
+  gp.k_tiles = d.k_tiles;
+  gp.k_per_split = d.k_per_split;
+  gp.splits = d.splits;
+  gp.units = d.tiles * d.splits;
+  gp.group_m = 8;
+  gp.stream_b = p.M <= 128 ? 1 : 0;  // one row tile: every weight byte is read once
+
+  if (int r = ensure_smem_attr(plan.config, dev)) return r;
+  const int grid = std::min(gp.units, sms);
+  e.launch(gp, grid, stream);
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) return cuda_fail(err, "GEMM kernel launch");
+  return BFP8_OK;
+}
+
+int64_t bfp8_device_status(int reset) {
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+  unsigned long long v = 0;
+  e = cudaMemcpyFromSymbol(&v, bfp8::g_status, sizeof(v));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyFromSymbol(status)");
+  if (reset && v) {
+    const unsigned long long zero = 0;
+    e = cudaMemcpyToSymbol(bfp8::g_status, &zero, sizeof(zero));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyToSymbol(status)");
+  }
+  return int64_t(v & 0x7fffffffffffffffull);
+}
+
+}  // extern "C"

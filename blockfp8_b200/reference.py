@@ -1,0 +1,70 @@
+"""Float64 statement of the block-scaled GEMM, and the error model.
+
+Public API the reference exports (blockfp8/reference.py:20-82); plain
+PyTorch on any device, never called by the CUDA path.  gemm() on CPU
+tensors raises and points here, as the reference does.
+
+Within one 128-wide K block the products of two e4m3 values are multiples
+of 2^-18 below 2^18 in magnitude, so a block's sum of 128 products is exact
+in float64 in any order; only the per-block scaling and the sum over blocks
+round, by at most 2^-53 relative each.
+"""
+
+import torch
+
+from .layout import BLOCK_N, GROUP_K, cdiv
+
+
+def _b_scales_per_row(b_scales: torch.Tensor, n: int) -> torch.Tensor:
+    return b_scales.repeat_interleave(BLOCK_N, dim=0)[:n]
+
+
+def reference_gemm(a_q, a_scales, b_q, b_scales, absolute: bool = False) -> torch.Tensor:
+    """C [M, N] float64.  absolute=True: sum_kb |sa sb| sum_k |a b| instead,
+    the magnitude accumulation-error bounds scale with."""
+    m, k = a_q.shape
+    n = b_q.shape[0]
+    a, b = a_q.double(), b_q.double()
+    sa, sb = a_scales.double(), _b_scales_per_row(b_scales.double(), n)
+    if absolute:
+        a, b, sa, sb = a.abs(), b.abs(), sa.abs(), sb.abs()
+    c = torch.zeros(m, n, dtype=torch.float64, device=a_q.device)
+    for kb in range(cdiv(k, GROUP_K)):
+        lo, hi = kb * GROUP_K, min(k, (kb + 1) * GROUP_K)
+        block = a[:, lo:hi] @ b[:, lo:hi].t()
+        c += block * (sa[:, kb:kb + 1] * sb[:, kb][None, :])
+    return c
+
+
+def dequantize_activations(x_q: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    """x_q [M, K] e4m3 with scales [M, ceil(K/128)] -> float64 [M, K]."""
+    k = x_q.shape[1]
+    return x_q.double() * scales.double().repeat_interleave(GROUP_K, dim=1)[:, :k]
+
+
+def dequantize_weights(w_q: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    """w_q [N, K] e4m3 with scales [ceil(N/128), ceil(K/128)] -> float64 [N, K]."""
+    n, k = w_q.shape
+    s = _b_scales_per_row(scales.double(), n).repeat_interleave(GROUP_K, dim=1)[:, :k]
+    return w_q.double() * s
+
+
+# The reference's worst-case model of its sm_89 MMA: 32 products plus the
+# accumulator aligned to the largest, MMA_FRACTION_BITS bits kept below it,
+# four MMAs per K block, then fp32 promotion.  Kept with the reference's
+# constant for API compatibility; the B200 tests bound errors with the
+# relative/absolute tolerance of the parity contract instead.
+MMA_FRACTION_BITS = 13
+BF16_U = 2.0 ** -8  # unit roundoff of bfloat16
+FP32_U = 2.0 ** -24
+
+
+def acc_gamma(k: int) -> float:
+    """Worst-case accumulation error relative to sum_kb |sa sb| sum_k |a b|."""
+    return 4 * 33 * 2.0 ** -MMA_FRACTION_BITS + (4 + 3 * cdiv(k, 128)) * FP32_U
+
+
+def error_bound(c_exact: torch.Tensor, c_abs: torch.Tensor, k: int) -> torch.Tensor:
+    """Elementwise bound on |C_kernel - C_exact| for a bf16 output."""
+    acc = acc_gamma(k) * c_abs
+    return BF16_U * (c_exact.abs() + acc) + acc + torch.finfo(torch.float32).tiny

@@ -1,0 +1,134 @@
+/*
+ * blockfp8_b200 -- C ABI of the B200 (sm_100a) block-FP8 linear hot path.
+ *
+ *   C[M, N] (bf16) = sum_kb sa[m, kb] * sb[n / 128, kb] * sum_{k in kb} A[m, k] * B[n, k]
+ *
+ * A [M, K] and B [N, K] are float8_e4m3fn codes, K-contiguous ("TN"); sa is
+ * float32 [M, ceil(K/128)] with any strides; sb is float32
+ * [ceil(N/128), ceil(K/128)]; C is bf16 [M, N].  All strides are in elements.
+ *
+ * This header is the drop-in replacement for the reference's host interface
+ * (simon-jd/blockfp8 csrc/blockfp8.h:17-76, a C++ namespace API used only by
+ * csrc/ops.cpp).  Each declaration names the reference function it replaces.
+ * Differences: plain C (extern "C"), structs passed by pointer, errors are
+ * returned as negative status codes with the message in bfp8_last_error()
+ * instead of a thrown std::runtime_error, and the CUDA stream is passed as
+ * void* (a cudaStream_t), so the header needs no CUDA include.
+ *
+ * Every pointer in a problem struct is a device pointer on the current CUDA
+ * device.  Launch functions are asynchronous on the given stream.
+ */
+#ifndef BLOCKFP8_B200_H
+#define BLOCKFP8_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BFP8_OK 0
+#define BFP8_EINVAL (-1)  /* bad argument: shape, alignment, config id, ... */
+#define BFP8_ECUDA (-2)   /* a CUDA runtime or driver call failed */
+
+/* Problem descriptor; replaces blockfp8::GemmProblem (csrc/blockfp8.h:17-30).
+ * With a fused plan, a points at bf16 activations [M, K] (row stride lda),
+ * which are quantized per row per 128-wide K group with the amax floored at
+ * eps; sa is then unused. */
+typedef struct bfp8_gemm_problem {
+  const void* a;
+  int64_t lda;
+  const void* b;
+  int64_t ldb;
+  const float* sa;
+  int64_t sa_m, sa_k;
+  const float* sb;
+  int64_t sb_n, sb_k;
+  void* c;
+  int64_t ldc;
+  int M, N, K;
+  float eps;
+} bfp8_gemm_problem;
+
+/* Kernel choice; replaces blockfp8::Plan (csrc/blockfp8.h:32-36). */
+typedef struct bfp8_plan {
+  int config; /* index into the compiled (fused, if fused) configurations */
+  int splits; /* K splits (1 = no split-K) */
+  int fused;  /* nonzero: A is bf16 and is quantized as part of the call */
+} bfp8_plan;
+
+/* Activation quantization problem; replaces blockfp8::QuantProblem
+ * (csrc/blockfp8.h:66-75): x [M, K] bf16 (row stride ldx) -> q [M, K] e4m3
+ * (row stride ldq) and one float scale per row per 128-wide K group at
+ * s[m * s_m + kb * s_k].  K must be a multiple of 8. */
+typedef struct bfp8_quant_problem {
+  const void* x;
+  int64_t ldx;
+  void* q;
+  int64_t ldq;
+  float* s;
+  int64_t s_m, s_k;
+  int M, K;
+  float eps;
+} bfp8_quant_problem;
+
+/* Configuration tables; replace num_configs / config_name / num_fused_configs
+ * / fused_config_name (csrc/blockfp8.h:38-41).  Names are static strings. */
+int bfp8_num_configs(void);
+const char* bfp8_config_name(int config);
+int bfp8_num_fused_configs(void);
+const char* bfp8_fused_config_name(int config);
+
+/* The built-in plan; replace choose_plan / choose_fused_plan
+ * (csrc/blockfp8.h:43-45).  num_sms = the device's multiprocessor count. */
+bfp8_plan bfp8_choose_plan(int M, int N, int K, int num_sms);
+bfp8_plan bfp8_choose_fused_plan(int M, int N, int K, int num_sms);
+
+/* Whether linear runs this shape through the fused path; replaces
+ * prefers_fused (csrc/blockfp8.h:47-50).  Returns 0 or 1. */
+int bfp8_prefers_fused(int M, int N, int K);
+
+/* Tiles and K tiles of a plan; replaces plan_shape (csrc/blockfp8.h:52-53).
+ * Returns BFP8_OK or BFP8_EINVAL (bad config id). */
+int bfp8_plan_shape(const bfp8_gemm_problem* p, bfp8_plan plan, int* tiles, int* k_tiles);
+
+/* Scratch of one launch: fp32 split-K partial tiles, preceded for a fused
+ * plan by the quantized activations and their scales (bytes); and the int
+ * split-K arrival counters.  Replace workspace_bytes / counters_needed
+ * (csrc/blockfp8.h:55-57).  Workspace is 0 for an unfused one-split plan,
+ * counters 0 for any one-split plan.  Negative on a bad config id. */
+int64_t bfp8_workspace_bytes(const bfp8_gemm_problem* p, bfp8_plan plan);
+int bfp8_counters_needed(const bfp8_gemm_problem* p, bfp8_plan plan);
+
+/* Launch the GEMM; replaces launch_gemm (csrc/blockfp8.h:59-61).
+ * workspace: bfp8_workspace_bytes() bytes (may be NULL when that is 0).
+ * counters: bfp8_counters_needed() ints that are zero on entry; the kernel
+ * leaves them zero.  Calls that overlap on the GPU must not share counters
+ * or workspace.  A fused plan quantizes p->a (bf16) into the front of the
+ * workspace first.  Returns BFP8_OK, BFP8_EINVAL or BFP8_ECUDA. */
+int bfp8_launch_gemm(const bfp8_gemm_problem* p, bfp8_plan plan, float* workspace, int* counters,
+                     void* stream);
+
+/* Launch the activation quantizer; replaces launch_quantize
+ * (csrc/blockfp8.h:76).  Returns BFP8_OK, BFP8_EINVAL or BFP8_ECUDA. */
+int bfp8_launch_quantize(const bfp8_quant_problem* p, void* stream);
+
+/* The message of the last failed call on this host thread ("" if none).
+ * No reference counterpart (the reference throws std::runtime_error). */
+const char* bfp8_last_error(void);
+
+/* Watchdog status of the current device: 0, or the code that the first
+ * kernel whose bounded wait on a barrier gave up wrote (the kernel then
+ * returned early instead of hanging).  Synchronises the device.  With
+ * reset != 0 the word is cleared.  No reference counterpart. */
+int64_t bfp8_device_status(int reset);
+
+/* ABI version of this header (1). */
+int bfp8_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BLOCKFP8_B200_H */

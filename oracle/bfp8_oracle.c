@@ -140,4 +140,13 @@ void oracle_e4m3_decode(const uint8_t* c, int64_t n, float* out) {
   for (int64_t i = 0; i < n; ++i) out[i] = oracle_e4m3_to_float(c[i]);
 }
 
+/* Decode straight to float64 (the GEMM's operand type); parallel, so the
+ * first touch of a large output array is spread over all threads. */
+void oracle_e4m3_decode_f64(const uint8_t* c, int64_t n, double* out) {
+  double table[256];
+  for (int i = 0; i < 256; ++i) table[i] = (double)oracle_e4m3_to_float((uint8_t)i);
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < n; ++i) out[i] = table[c[i]];
+}
+
 int oracle_abi_version(void) { return 1; }

@@ -59,6 +59,8 @@ def lib() -> ctypes.CDLL:
         L.oracle_quantize_weights.restype = None
         L.oracle_e4m3_decode.argtypes = [u8p, i64, f32p]
         L.oracle_e4m3_decode.restype = None
+        L.oracle_e4m3_decode_f64.argtypes = [u8p, i64, ctypes.POINTER(ctypes.c_double)]
+        L.oracle_e4m3_decode_f64.restype = None
         L.oracle_e4m3_from_float.argtypes = [ctypes.c_float]
         L.oracle_e4m3_from_float.restype = ctypes.c_uint8
         _lib = L
@@ -81,6 +83,14 @@ def e4m3_decode(codes: np.ndarray) -> np.ndarray:
     c = np.ascontiguousarray(codes, dtype=np.uint8)
     out = np.empty(c.shape, dtype=np.float32)
     lib().oracle_e4m3_decode(_ptr(c, ctypes.c_uint8), c.size, _ptr(out, ctypes.c_float))
+    return out
+
+
+def e4m3_decode_f64(codes: np.ndarray) -> np.ndarray:
+    """float8_e4m3fn codes (uint8) -> float64, exactly."""
+    c = np.ascontiguousarray(codes, dtype=np.uint8)
+    out = np.empty(c.shape, dtype=np.float64)
+    lib().oracle_e4m3_decode_f64(_ptr(c, ctypes.c_uint8), c.size, _ptr(out, ctypes.c_double))
     return out
 
 
@@ -142,8 +152,8 @@ def reference_gemm(a_q, a_scales, b_q, b_scales, absolute: bool = False) -> np.n
     c += block * (sa * sb), each step rounded separately in float64."""
     m, k = a_q.shape
     n = b_q.shape[0]
-    a = e4m3_decode(a_q).astype(np.float64)
-    b = e4m3_decode(b_q).astype(np.float64)
+    a = e4m3_decode_f64(a_q)
+    b = e4m3_decode_f64(b_q)
     sa = np.asarray(a_scales, dtype=np.float64)
     sb = _expand_b_scales(np.asarray(b_scales, dtype=np.float64), n)
     if absolute:

@@ -1,0 +1,102 @@
+"""Parity through the C ABI alone (ctypes on libblockfp8_b200.so, no torch ops),
+against the CPU oracle, on the BASELINE shapes.
+
+Sizes: the four Qwen3-8B linear shapes at decode M (full outputs checked
+against the oracle) and at prefill M (a row sample against the oracle, plus
+the size-independent property that each output row depends only on its own
+input row: the first rows of a large call equal a small call bitwise).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from blockfp8_b200 import _native, capi
+from helpers import (FP8, assert_close, assert_exact, bf16_activations, codes, f32,
+                     integer_operands, oracle_gemm, oracle_quant)
+from oracle import oracle as O
+
+pytestmark = [
+    pytest.mark.gpu,
+    pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA GPU"),
+]
+
+DEV = "cuda"
+SHAPES = {"qkv": (6144, 4096), "o": (4096, 4096), "gate_up": (24576, 4096), "down": (4096, 12288)}
+
+
+def _weights(n, k, seed=0):
+    """w ~ N(0, 0.02) on a CPU generator, quantized by the oracle."""
+    g = torch.Generator().manual_seed(seed)
+    b, sb = O.quantize_weights((torch.randn(n, k, generator=g) * 0.02).numpy())
+    return b, sb, torch.from_numpy(b).view(FP8).to(DEV), torch.from_numpy(sb).to(DEV)
+
+
+def test_library_reports_itself():
+    lib = _native.capi()
+    assert lib.bfp8_abi_version() == 1
+    assert lib.bfp8_num_configs() >= 1
+    assert capi.choose_plan(1, 6144, 4096, 148).splits >= 1
+
+
+@pytest.mark.parametrize("m", [1, 7, 33])
+def test_quantize_through_c_abi(m):
+    x = bf16_activations(m, 4096, seed=m, ties=m == 7)
+    q, s = capi.quantize(x.to(DEV))
+    q2, s2 = oracle_quant(x)
+    assert np.array_equal(codes(q), q2) and np.array_equal(f32(s), s2)
+
+
+@pytest.mark.parametrize("layer", sorted(SHAPES))
+@pytest.mark.parametrize("m", [1, 2, 4, 8, 16, 32])
+def test_decode_shapes_full_output(layer, m):
+    n, k = SHAPES[layer]
+    b_np, sb_np, b, sb = _weights(n, k, seed=1)
+    x = bf16_activations(m, k, seed=100 + m, scale=1.0)
+    q, s = capi.quantize(x.to(DEV))
+    c = capi.gemm(q, s, b, sb)
+    a_np, sa_np = oracle_quant(x)
+    assert np.array_equal(codes(q), a_np)
+    assert_close(c, O.reference_gemm(a_np, sa_np, b_np, sb_np))
+    # the fused route gives the same bits under the same plan
+    assert torch.equal(capi.gemm(x.to(DEV), None, b, sb, fused=True), c)
+
+
+@pytest.mark.parametrize("layer", sorted(SHAPES))
+def test_prefill_shapes_row_sample_and_row_independence(layer):
+    n, k = SHAPES[layer]
+    m = 4096 if layer != "gate_up" else 8192
+    b_np, sb_np, b, sb = _weights(n, k, seed=2)
+    x = bf16_activations(m, k, seed=7, scale=1.0).to(DEV)
+    q, s = capi.quantize(x)
+    c = capi.gemm(q, s, b, sb)
+    rows = np.r_[0:64, m - 64:m, np.random.default_rng(0).integers(0, m, 64)]
+    a_np = codes(q)[rows]
+    sa_np = f32(s)[rows]
+    assert_close(c[torch.from_numpy(rows).to(DEV)], O.reference_gemm(a_np, sa_np, b_np, sb_np))
+    # Each output row depends only on its own activation row: under the
+    # large call's plan, a 256-row call reproduces its first rows bitwise.
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    plan = capi.choose_plan(m, n, k, sms)
+    c_small = capi.gemm(q[:256], s[:256], b, sb, config=plan.config, splits=plan.splits)
+    assert torch.equal(c[:256], c_small)
+
+
+@pytest.mark.parametrize("splits", [1, 2, 5])
+def test_exact_integer_through_c_abi(splits):
+    a, sa, b, sb = integer_operands(77, 1032, 1040, seed=splits)
+    assert_exact(capi.gemm(a, sa, b, sb, config=1, splits=splits), oracle_gemm(a, sa, b, sb))
+
+
+def test_bad_arguments_come_back_as_errors():
+    a, sa, b, sb = integer_operands(4, 256, 256)
+    c = torch.empty(4, 256, dtype=torch.bfloat16, device=DEV)
+    p = capi.problem(a, sa, b, sb, c)
+    p.K = 200  # not a multiple of 16
+    with pytest.raises(RuntimeError, match="K must be"):
+        capi.launch_gemm(p, capi.choose_plan(4, 256, 256, 148))
+    p = capi.problem(a, sa, b, sb, c)
+    plan = capi.choose_plan(4, 256, 256, 148)
+    plan.config = 99
+    with pytest.raises(RuntimeError, match="config"):
+        capi.launch_gemm(p, plan)
