@@ -45,6 +45,7 @@ int cdiv(int a, int b) { return (a + b - 1) / b; }
 struct ConfigEntry {
   const char* name;
   int bn, stages, threads, smem;
+  bool swap;  // MMA rows are weight rows, columns are tokens (decode)
   const void* kernel;
   void (*launch)(const GemmParams&, int grid, cudaStream_t);
 };
@@ -56,19 +57,23 @@ void launch_cfg(const GemmParams& gp, int grid, cudaStream_t stream) {
 
 template <class Cfg>
 ConfigEntry entry(const char* name) {
-  return {name, Cfg::BN, Cfg::STAGES, Cfg::THREADS, Cfg::SMEM_BYTES,
+  return {name, Cfg::BN, Cfg::STAGES, Cfg::THREADS, Cfg::SMEM_BYTES, Cfg::SWAP,
           reinterpret_cast<const void*>(&gemm_kernel<Cfg>), &launch_cfg<Cfg>};
 }
 
-//                        BN  stages
-using Cfg256 = GemmCfg<256, 4>;
-using Cfg128 = GemmCfg<128, 6>;
-using Cfg64 = GemmCfg<64, 8>;
+// Normal order: "m128n<BN>": 128 activation rows x BN weight rows per tile.
+// Swapped order: "w128t<BN>": 128 weight rows x BN tokens per tile (decode).
+//                        BN  stages  swapped
+using Cfg256 = GemmCfg<256, 4, false>;
+using Cfg128 = GemmCfg<128, 6, false>;
+using Cfg64 = GemmCfg<64, 8, false>;
+using CfgW16 = GemmCfg<16, 10, true>;
+using CfgW32 = GemmCfg<32, 10, true>;
+using CfgW64 = GemmCfg<64, 8, true>;
 
 const ConfigEntry kConfigs[] = {
-    entry<Cfg256>("m128n256s4"),
-    entry<Cfg128>("m128n128s6"),
-    entry<Cfg64>("m128n64s8"),
+    entry<Cfg256>("m128n256s4"), entry<Cfg128>("m128n128s6"), entry<Cfg64>("m128n64s8"),
+    entry<CfgW16>("w128t16s10"), entry<CfgW32>("w128t32s10"), entry<CfgW64>("w128t64s8"),
 };
 constexpr int kNumConfigs = int(sizeof(kConfigs) / sizeof(kConfigs[0]));
 // The fused path (gemm_bf16) quantizes into the workspace, then runs the
@@ -129,7 +134,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 int make_map(CUtensorMap* map, CUtensorMapDataType dtype, const void* ptr, uint64_t inner,
-             uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer) {
+             uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+             CUtensorMapSwizzle swizzle) {
   auto fn = encode_fn();
   if (!fn) return fail(BFP8_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
   const cuuint64_t dims[2] = {inner, outer};
@@ -137,7 +143,7 @@ int make_map(CUtensorMap* map, CUtensorMapDataType dtype, const void* ptr, uint6
   const cuuint32_t box[2] = {box_inner, box_outer};
   const cuuint32_t estrides[2] = {1, 1};
   CUresult r = fn(map, dtype, 2, const_cast<void*>(ptr), dims, strides, box, estrides,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(BFP8_ECUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
   return BFP8_OK;
@@ -189,18 +195,22 @@ double plan_cost_ns(int M, int N, int K, int num_sms, int config, int splits) {
   const int k_tiles = cdiv(K, 128);
   const int per = cdiv(k_tiles, std::max(1, std::min(splits, k_tiles)));
   const int real_splits = cdiv(k_tiles, per);
-  const int tiles_m = cdiv(M, 128), tiles_n = cdiv(N, e.bn);
-  const int64_t units = int64_t(tiles_m) * tiles_n * real_splits;
+  const int rows_total = e.swap ? N : M, cols_total = e.swap ? M : N;
+  const int tiles_r = cdiv(rows_total, 128), tiles_c = cdiv(cols_total, e.bn);
+  const int64_t units = int64_t(tiles_r) * tiles_c * real_splits;
   const int64_t waves = (units + num_sms - 1) / num_sms;
   const int active = int(std::min<int64_t>(units, num_sms));
   const double clk_ghz = 1.8;
   const double mma_ns = 2.0 * e.bn / clk_ghz;
-  const int rows = std::min(M, 128);
-  const double bytes = double(rows) * 128 + double(std::min(N, e.bn)) * 128;
+  const int rows = std::min(rows_total, 128);
+  const double bytes = double(rows) * 128 + double(std::min(cols_total, e.bn)) * 128;
   const double hbm_gbs = 6500.0, l2_sm_gbs = 120.0;
   const double sm_gbs = std::min(l2_sm_gbs, hbm_gbs / active);
   const double load_ns = bytes / sm_gbs;
-  double t = double(waves) * per * std::max(mma_ns, load_ns);
+  // The promotion of a K block: each warp that owns valid rows loads its
+  // columns from TMEM in 32-column chunks, one after another.
+  const double epi_ns = 40.0 + 60.0 * std::max(1, std::min(e.bn, e.swap ? e.bn : 128) / 32);
+  double t = double(waves) * per * std::max(std::max(mma_ns, load_ns), epi_ns);
   const double tile_out = double(rows) * e.bn;
   t += double(waves) * tile_out * 2 / (hbm_gbs / active) * 1.0;  // bf16 store
   if (real_splits > 1) t += double(waves) * tile_out * 4 * 2 / sm_gbs + 600.0;
@@ -247,15 +257,15 @@ const TableEntry* balanced_entry(const TableEntry* above, int M, int N, int K, i
 }
 
 struct Derived {
-  int tiles_m, tiles_n, tiles, k_tiles, k_per_split, splits;
+  int tiles_r, tiles_c, tiles, k_tiles, k_per_split, splits;
 };
 
 Derived derive(const bfp8_gemm_problem& p, const bfp8_plan& plan) {
   const ConfigEntry& e = kConfigs[plan.config];
   Derived d;
-  d.tiles_m = cdiv(p.M, 128);
-  d.tiles_n = cdiv(p.N, e.bn);
-  d.tiles = d.tiles_m * d.tiles_n;
+  d.tiles_r = cdiv(e.swap ? p.N : p.M, 128);
+  d.tiles_c = cdiv(e.swap ? p.M : p.N, e.bn);
+  d.tiles = d.tiles_r * d.tiles_c;
   d.k_tiles = cdiv(p.K, 128);
   const int splits = std::max(1, std::min(plan.splits, d.k_tiles));
   d.k_per_split = cdiv(d.k_tiles, splits);
@@ -297,11 +307,9 @@ int check_problem(const bfp8_gemm_problem& p, bool fused) {
 }
 
 int launch_quant(const QuantParams& qp, cudaStream_t stream, int num_sms) {
-  const int64_t groups = int64_t(qp.M) * qp.kb;
-  if (groups == 0) return BFP8_OK;
-  const int64_t per_cta = kQuantThreads / 16;
-  const int64_t want = (groups + per_cta - 1) / per_cta;
-  const int grid = int(std::min<int64_t>(want, int64_t(num_sms) * 8));
+  const int64_t tasks = int64_t(cdiv(qp.M, kQuantRows)) * cdiv(qp.kb, kQuantGroups);
+  if (tasks == 0) return BFP8_OK;
+  const int grid = int(std::min<int64_t>(tasks, int64_t(num_sms) * 8));
   quantize_kernel<<<grid, kQuantThreads, 0, stream>>>(qp);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "quantize kernel launch");
@@ -423,14 +431,27 @@ int bfp8_launch_gemm(const bfp8_gemm_problem* pp, bfp8_plan plan, float* workspa
   const ConfigEntry& e = kConfigs[plan.config];
   GemmParams gp;
   std::memset(&gp, 0, sizeof(gp));
-  if (int r = make_map(&gp.map_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.a, uint64_t(p.K), uint64_t(p.M),
-                       uint64_t(p.lda), 128, 128))
+  // Operand tiles: 128 rows of the MMA A operand, BN rows of the B operand,
+  // one 128-byte K block each, 128-byte swizzle.  Activations are A in the
+  // normal order and B in the swapped one.
+  const void* a_src = e.swap ? p.b : p.a;
+  const void* b_src = e.swap ? p.a : p.b;
+  const int64_t a_ld = e.swap ? p.ldb : p.lda, b_ld = e.swap ? p.lda : p.ldb;
+  const int a_rows = e.swap ? p.N : p.M, b_rows = e.swap ? p.M : p.N;
+  if (int r = make_map(&gp.map_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, a_src, uint64_t(p.K),
+                       uint64_t(a_rows), uint64_t(a_ld), 128, 128, CU_TENSOR_MAP_SWIZZLE_128B))
     return r;
-  if (int r = make_map(&gp.map_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.b, uint64_t(p.K), uint64_t(p.N),
-                       uint64_t(p.ldb), 128, uint32_t(e.bn)))
+  if (int r = make_map(&gp.map_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, b_src, uint64_t(p.K),
+                       uint64_t(b_rows), uint64_t(b_ld), 128, uint32_t(e.bn),
+                       CU_TENSOR_MAP_SWIZZLE_128B))
     return r;
-  if (int r = make_map(&gp.map_c, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.c, uint64_t(p.N),
-                       uint64_t(p.M), uint64_t(p.ldc) * 2, 64, 32))
+  // Output: normal order stores [32 rows x 32 columns] chunks (64-byte
+  // swizzle); swapped order stores [BN tokens x 32 columns] tiles.
+  if (int r = e.swap ? make_map(&gp.map_c, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.c, uint64_t(p.N),
+                                uint64_t(p.M), uint64_t(p.ldc) * 2, 32, uint32_t(e.bn),
+                                CU_TENSOR_MAP_SWIZZLE_NONE)
+                     : make_map(&gp.map_c, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.c, uint64_t(p.N),
+                                uint64_t(p.M), uint64_t(p.ldc) * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
     return r;
   gp.sa = p.sa;
   gp.sa_m = p.sa_m;
@@ -443,15 +464,20 @@ int bfp8_launch_gemm(const bfp8_gemm_problem* pp, bfp8_plan plan, float* workspa
   gp.M = p.M;
   gp.N = p.N;
   gp.K = p.K;
-  gp.tiles_m = d.tiles_m;
-  gp.tiles_n = d.tiles_n;
+  gp.tiles_r = d.tiles_r;
+  gp.tiles_c = d.tiles_c;
   gp.tiles = d.tiles;
   gp.k_tiles = d.k_tiles;
   gp.k_per_split = d.k_per_split;
   gp.splits = d.splits;
   gp.units = d.tiles * d.splits;
-  gp.group_m = 8;
-  gp.stream_b = p.M <= 128 ? 1 : 0;  // one row tile: every weight byte is read once
+  // Raster: when all row tiles of the MMA A operand fit comfortably in L2,
+  // sweep them all for each column tile, so A stays resident and B streams
+  // from HBM once; otherwise groups of 8 row tiles (the reference's
+  // group_m).  Swapped order: A is the weights, B the few token rows.
+  const int64_t a_bytes = int64_t(d.tiles_r) * 128 * p.K;
+  gp.group_r = e.swap || a_bytes <= (int64_t(48) << 20) ? d.tiles_r : 8;
+  gp.stream_b = (e.swap || p.M <= 128) ? 1 : 0;  // weights read once: evict them first
 
   if (int r = ensure_smem_attr(plan.config, dev)) return r;
   const int grid = std::min(gp.units, sms);

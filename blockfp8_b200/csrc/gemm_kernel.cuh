@@ -3,33 +3,42 @@
 //   C[m, n] = sum_kb sa[m, kb] * sb[n / 128, kb] * sum_{k in kb} A[m, k] * B[n, k]
 //
 // One persistent, warp-specialised CTA per SM walks a static list of work
-// units (an output tile of 128 x BN and a range of 128-wide K blocks):
+// units (an output tile and a range of 128-wide K blocks):
 //
-//   warp 0      TMA producer: A tile [128 x 128 B] and B tile [BN x 128 B]
-//               of each K block into a STAGES-deep shared-memory ring
-//               (128-byte swizzle), completion counted in bytes on the
-//               stage's "full" mbarrier;
+//   warp 0      TMA producer: the two operand tiles of each K block
+//               (128-byte swizzle, 128 bytes = one K block per row) into a
+//               STAGES-deep shared-memory ring; completion is counted in
+//               bytes on the stage's "full" mbarrier;
 //   warp 1      MMA issuer (one thread): per K block, four
 //               tcgen05.mma.kind::f8f6f4 (K = 32 each, e4m3 x e4m3 -> f32)
 //               into one of ACC_BUFS tensor-memory (TMEM) partial buffers,
 //               the first with the accumulator input disabled, so the buffer
 //               holds exactly that block's unscaled partial sums; then
 //               tcgen05.commit frees the smem stage and publishes the buffer;
-//   warps 2..   promotion + epilogue (EPI_WG warpgroups; warp w reads TMEM
+//   warps 4..   promotion + epilogue (EPI_WG warpgroups; warp w reads TMEM
 //               lanes 32 * (w % 4) ..): tcgen05.ld the partial, multiply by
-//               sa[m, kb] * sb[nb, kb] and add into fp32 registers with one
-//               fmaf per value (the promotion of the reference kernel,
-//               blockfp8 csrc/gemm_kernel.cuh:372-382, same operation
-//               order), release the buffer; after the unit's last K block,
-//               round to bf16 into a swizzled smem tile and TMA-store it.
+//               the block's scale sa[m, kb] * sb[nb, kb] and add into fp32
+//               registers with one fmaf per value -- the promotion of the
+//               reference kernel (blockfp8 csrc/gemm_kernel.cuh:372-382), in
+//               the same operation order -- and release the buffer.  Scales
+//               are prefetched PF K blocks ahead.  After the unit's last K
+//               block: round to bf16 into a swizzled smem tile, TMA store.
+//
+// Two operand orders.  Normal (prefill): the MMA's 128 rows are activation
+// rows and its N = BN columns are weight rows.  Swapped (decode, SWAP): the
+// 128 MMA rows are weight rows and N = BN (16..64) are tokens, so a decode
+// batch of M <= 64 tokens does not waste 128-row MMAs and the promotion of
+// a K block is spread over all 128 TMEM lanes (4 warps) instead of the one
+// warp that may read lanes 0-31.  Every output element is the same sum of
+// the same products in both orders.
 //
 // Because every K block gets its own TMEM buffer, the MMAs of block k + 1
-// run while block k is being promoted.  With split-K the units of one tile
-// cover disjoint K ranges; each writes its fp32 partial tile to a workspace
-// and the last to arrive (an atomic counter) sums the partials in split order
+// run while block k is promoted.  With split-K the units of one tile cover
+// disjoint K ranges; each writes its fp32 partial tile to a workspace and
+// the last to arrive (an atomic counter) sums the partials in split order
 // 0, 1, ..., S - 1 and stores the tile, as the reference does
-// (blockfp8 csrc/gemm_kernel.cuh:403-448), so results are deterministic and
-// no CTA ever waits for another.
+// (blockfp8 csrc/gemm_kernel.cuh:403-448): deterministic, no CTA waits for
+// another.
 //
 // Every mbarrier wait is bounded (ptx.cuh): on a timeout the kernel records a
 // status code, drains its in-flight copies and MMAs, frees TMEM and returns.
@@ -45,44 +54,62 @@
 namespace bfp8 {
 
 struct GemmParams {
-  CUtensorMap map_a;  // A e4m3 [M, K] (row stride lda), box 128 x 128, 128B swizzle
-  CUtensorMap map_b;  // B e4m3 [N, K] (row stride ldb), box 128 x BN, 128B swizzle
-  CUtensorMap map_c;  // C bf16 [M, N] (row stride ldc), box 64 x 32, 128B swizzle
+  CUtensorMap map_a;  // MMA A operand (128-row tiles): activations, or weights when swapped
+  CUtensorMap map_b;  // MMA B operand (BN-row tiles): weights, or activations when swapped
+  CUtensorMap map_c;  // C bf16 [M, N]
   const float* sa;
   int64_t sa_m, sa_k;
   const float* sb;
   int64_t sb_n, sb_k;
-  float* workspace;  // split-K partial tiles: [splits][tiles][128][BN] fp32
+  float* workspace;  // split-K partial tiles: [splits][tiles][128 * BN] fp32
   int* counters;     // split-K arrivals, one per tile, zero between launches
   int M, N, K;
-  int tiles_m, tiles_n, tiles;
+  int tiles_r, tiles_c, tiles;  // tiles over the MMA rows (128) and columns (BN)
   int k_tiles, k_per_split, splits;
-  int units;  // tiles * splits
-  int group_m;
-  int stream_b;  // 1: B is read once (decode), hint L2 to evict it first
+  int units;    // tiles * splits
+  int group_r;  // raster: groups of group_r row tiles, rows fastest inside a group
+  int stream_b;  // 1: weights are read once (decode): L2 evict-first for them
 };
 
-template <int BN_, int STAGES_>
+template <int BN_, int STAGES_, bool SWAP_>
 struct GemmCfg {
   static constexpr int BM = 128, BN = BN_, BK = 128, STAGES = STAGES_;
-  static_assert(BN == 64 || BN == 128 || BN == 256, "MMA N of 64, 128 or 256");
-  static constexpr int COLS = BN < 128 ? BN : 128;  // accumulators per epilogue thread
-  static constexpr int EPI_WG = BN / COLS;
+  static constexpr bool SWAP = SWAP_;
+  static_assert(SWAP ? (BN == 16 || BN == 32 || BN == 64) : (BN == 64 || BN == 128 || BN == 256),
+                "unsupported tile");
+  static constexpr int COLS = SWAP ? BN : (BN < 128 ? BN : 128);  // accumulators per thread
+  static constexpr int EPI_WG = SWAP ? 1 : BN / COLS;
   static constexpr int EPI_WARPS = 4 * EPI_WG;
   static constexpr int EPI_THREADS = 32 * EPI_WARPS;
-  static constexpr int THREADS = 64 + EPI_THREADS;
+  // Warpgroup 0: warp 0 TMA, warp 1 MMA, warps 2-3 idle; warpgroups 1.. the
+  // epilogue, so registers can move between the roles by warpgroup.
+  static constexpr int THREADS = 128 + EPI_THREADS;
+  // Register split (setmaxnreg) when the launch share is too small for the
+  // epilogue's 128 accumulators: warpgroup 0 gives up all but REG_LOW.
+  static constexpr int REGS_LAUNCH = (65536 / THREADS) / 8 * 8 > 255 ? 255 : (65536 / THREADS) / 8 * 8;
+  static constexpr int REG_LOW = 40;
+  static constexpr int REG_HIGH =
+      ((REGS_LAUNCH * THREADS - 128 * REG_LOW) / EPI_THREADS) / 8 * 8 > 255
+          ? 248
+          : ((REGS_LAUNCH * THREADS - 128 * REG_LOW) / EPI_THREADS) / 8 * 8;
+  static constexpr bool SPLIT_REGS = REGS_LAUNCH < 200;
+  static_assert(!SPLIT_REGS || 128 * REG_LOW + EPI_THREADS * REG_HIGH <= REGS_LAUNCH * THREADS,
+                "register split exceeds the launch allocation");
   static constexpr int ACC_BUFS = 512 / BN > 4 ? 4 : 512 / BN;
-  static constexpr int TMEM_COLS = ACC_BUFS * BN;  // 256 or 512: a power of two >= 32
+  static constexpr int TMEM_COLS = ACC_BUFS * BN < 32 ? 32 : ACC_BUFS * BN;
   static constexpr int A_BYTES = BM * BK;
   static constexpr int B_BYTES = BN * BK;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int OUT_BYTES = 32 * 128;  // per epilogue warp: 32 rows x 64 bf16
+  // Output staging per epilogue warp: normal, two [32 rows x 32 bf16] chunk
+  // buffers (64-byte swizzle); swapped, one [BN tokens x 32 bf16] tile.
+  static constexpr int OUT_BYTES = SWAP ? BN * 64 : 2 * 32 * 64;
   static constexpr int SMEM_TILES = STAGES * STAGE_BYTES;
-  static constexpr int SMEM_OUT = EPI_WARPS * OUT_BYTES;
+  static constexpr int SMEM_OUT = ((EPI_WARPS * OUT_BYTES + 1023) / 1024) * 1024;
   static constexpr int NUM_BARS = 2 * STAGES + 2 * ACC_BUFS + 1;
   static constexpr int SMEM_BYTES = 1024 + SMEM_TILES + SMEM_OUT + NUM_BARS * 8 + 16;
   static_assert(SMEM_BYTES <= 232448, "more shared memory than one sm_100 CTA can have");
-  static_assert(TMEM_COLS <= 512, "TMEM has 512 columns");
+  static_assert(TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM allocation");
+  static_assert(STAGE_BYTES % 1024 == 0, "stages must stay 1024-byte aligned");
 };
 
 enum WaitSite : uint32_t {
@@ -95,28 +122,48 @@ enum WaitSite : uint32_t {
 };
 
 struct UnitCoord {
-  int tile, tm, tn, kt0, kt1, split;
+  int tile, tr, tc, kt0, kt1, split;
 };
 
-// Unit u = split * tiles + tile; tiles are rasterised in groups of group_m
-// tile rows (the reference's order, blockfp8 csrc/gemm_kernel.cuh:120-125).
+// Unit u = split * tiles + tile.  Tiles are rasterised in groups of group_r
+// row tiles, row tiles fastest inside a group (the reference's order,
+// blockfp8 csrc/gemm_kernel.cuh:120-125); the host picks group_r so the
+// operand that is re-read stays in L2.
 __device__ __forceinline__ UnitCoord unit_coord(const GemmParams& p, int u) {
   UnitCoord c;
   c.tile = u % p.tiles;
   c.split = u / p.tiles;
-  const int span = p.group_m * p.tiles_n;
-  const int first_m = (c.tile / span) * p.group_m;
-  const int rows = min(p.tiles_m - first_m, p.group_m);
-  c.tm = first_m + (c.tile % span) % rows;
-  c.tn = (c.tile % span) / rows;
+  const int span = p.group_r * p.tiles_c;
+  const int first = (c.tile / span) * p.group_r;
+  const int rows = min(p.tiles_r - first, p.group_r);
+  c.tr = first + (c.tile % span) % rows;
+  c.tc = (c.tile % span) / rows;
   c.kt0 = c.split * p.k_per_split;
   c.kt1 = min(p.k_tiles, c.kt0 + p.k_per_split);
   return c;
 }
 
+template <int N>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, float (&v)[N]);
+template <>
+__device__ __forceinline__ void tmem_ld<32>(uint32_t taddr, float (&v)[32]) {
+  tmem_ld32(taddr, v);
+}
+template <>
+__device__ __forceinline__ void tmem_ld<16>(uint32_t taddr, float (&v)[16]) {
+  tmem_ld16(taddr, v);
+}
+
+__device__ __forceinline__ uint32_t bf16x2_bits(float lo, float hi) {
+  __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&b);
+}
+
 template <class Cfg>
 __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_constant__ GemmParams p) {
   constexpr int BN = Cfg::BN, STAGES = Cfg::STAGES, ACC_BUFS = Cfg::ACC_BUFS, COLS = Cfg::COLS;
+  constexpr bool SWAP = Cfg::SWAP;
+  constexpr int PF = 4;  // scale prefetch distance in K blocks
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -163,11 +210,17 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
   tc_fence_after();
   const uint32_t tmem_base = misc[0];
 
+  if (warp < 4) {
+    if constexpr (Cfg::SPLIT_REGS) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(Cfg::REG_LOW));
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      const uint64_t pol_a = policy_evict_last();
-      const uint64_t pol_b = p.stream_b ? policy_evict_first() : policy_evict_normal();
+      // Activations are re-read by many tiles: keep them; weights streamed
+      // once (decode) go first.
+      const uint64_t pol_act = policy_evict_last();
+      const uint64_t pol_wgt = p.stream_b ? policy_evict_first() : policy_evict_normal();
+      const uint64_t pol_a = SWAP ? pol_wgt : pol_act;
+      const uint64_t pol_b = SWAP ? pol_act : pol_wgt;
       int stage = 0;
       uint32_t phase = 0;
       int issued = 0;
@@ -181,8 +234,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
           }
           const uint32_t dst = s_tiles + uint32_t(stage) * Cfg::STAGE_BYTES;
           mbar_arrive_expect_tx(full(stage), Cfg::STAGE_BYTES);
-          tma_load_2d(dst, &p.map_a, kt * 128, c.tm * 128, full(stage), pol_a);
-          tma_load_2d(dst + Cfg::A_BYTES, &p.map_b, kt * 128, c.tn * BN, full(stage), pol_b);
+          tma_load_2d(dst, &p.map_a, kt * 128, c.tr * 128, full(stage), pol_a);
+          tma_load_2d(dst + Cfg::A_BYTES, &p.map_b, kt * 128, c.tc * BN, full(stage), pol_b);
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -244,76 +297,136 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
       mbar_wait(mma_done, 0, nullptr, kWaitMmaDone);
     }
     __syncwarp();
+  }
   } else {
+    if constexpr (Cfg::SPLIT_REGS) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(Cfg::REG_HIGH));
     // ------------------------------------------------------------ promotion + epilogue
-    const int ew = warp - 2;     // epilogue warp 0 .. EPI_WARPS - 1
-    const int g = ew >> 2;       // warpgroup: column block g * COLS .. + COLS
-    const int quarter = warp & 3;  // TMEM lanes (= tile rows) 32 * quarter ..
+    const int ew = warp - 4;        // epilogue warp 0 .. EPI_WARPS - 1
+    const int g = ew >> 2;          // warpgroup: column block g * COLS .. + COLS
+    const int quarter = warp & 3;   // TMEM lanes (= tile rows) 32 * quarter ..
     const int row = 32 * quarter + lane;
     const uint32_t t_lane = tmem_base + (uint32_t(32 * quarter) << 16);
     const uint32_t out_buf = s_out + uint32_t(ew) * Cfg::OUT_BYTES;
+    const int rows_total = SWAP ? p.N : p.M;  // extent of the MMA row dimension
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
+    int out_chunk = 0;  // normal mode: alternates between the two staging buffers
 
     for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
       const UnitCoord c = unit_coord(p, u);
-      const int m = c.tm * 128 + row;
-      const bool row_ok = m < p.M;
-      const bool warp_rows = c.tm * 128 + 32 * quarter < p.M;  // warp-uniform
-      const int col0 = c.tn * BN + g * COLS;
-      const bool cols_ok = col0 < p.N;                         // warp-uniform
-      const float* sap = p.sa + int64_t(row_ok ? m : 0) * p.sa_m;
-      const float* sbp = p.sb + int64_t(cols_ok ? col0 / 128 : 0) * p.sb_n;
+      const int r = c.tr * 128 + row;                       // this thread's MMA row
+      const bool row_ok = r < rows_total;
+      const bool warp_rows = c.tr * 128 + 32 * quarter < rows_total;  // warp-uniform
+      const int col0 = c.tc * BN + g * COLS;                // first MMA column of this thread
+      const int cols_total = SWAP ? p.M : p.N;
+      const bool cols_ok = col0 < cols_total;               // warp-uniform
+      const bool work = warp_rows && cols_ok;
+
+      // Scale sources.  Normal: sa per row (thread), sb per 128-column block
+      // (warpgroup).  Swapped: sb per 128-row tile (CTA), sa per token
+      // column; lane j loads token col0 + j (and col0 + 32 + j when BN = 64).
+      const float* sa_ptr;
+      const float* sa2_ptr = nullptr;
+      const float* sb_ptr;
+      bool sa_ok, sa2_ok = false, sb_ok;
+      if constexpr (!SWAP) {
+        sa_ok = row_ok;
+        sa_ptr = p.sa + int64_t(row_ok ? r : 0) * p.sa_m;
+        sb_ok = cols_ok;
+        sb_ptr = p.sb + int64_t(cols_ok ? col0 / 128 : 0) * p.sb_n;
+      } else {
+        const int t0 = col0 + lane, t1 = col0 + 32 + lane;
+        sa_ok = t0 < p.M && lane < BN;
+        sa_ptr = p.sa + int64_t(sa_ok ? t0 : 0) * p.sa_m;
+        if constexpr (BN > 32) {
+          sa2_ok = t1 < p.M;
+          sa2_ptr = p.sa + int64_t(sa2_ok ? t1 : 0) * p.sa_m;
+        }
+        sb_ok = true;  // the tile's weight block exists (tr * 128 < N)
+        sb_ptr = p.sb + int64_t(c.tr) * p.sb_n;
+      }
+      float pa[PF], pa2[PF], pb[PF];
+      auto load_scales = [&](int kt, int j) {
+        pa[j] = sa_ok ? __ldg(sa_ptr + int64_t(kt) * p.sa_k) : 0.f;
+        if constexpr (SWAP && BN > 32) pa2[j] = sa2_ok ? __ldg(sa2_ptr + int64_t(kt) * p.sa_k) : 0.f;
+        pb[j] = sb_ok ? __ldg(sb_ptr + int64_t(kt) * p.sb_k) : 0.f;
+      };
+#pragma unroll
+      for (int j = 0; j < PF; ++j)
+        if (c.kt0 + j < c.kt1) load_scales(c.kt0 + j, j);
 
       float accum[COLS];
 #pragma unroll
       for (int j = 0; j < COLS; ++j) accum[j] = 0.f;
 
-      float sa_next = 0.f, sb_next = 0.f;
-      if (c.kt0 < c.kt1) {
-        if (row_ok) sa_next = __ldg(sap + int64_t(c.kt0) * p.sa_k);
-        if (cols_ok) sb_next = __ldg(sbp + int64_t(c.kt0) * p.sb_k);
-      }
-      for (int kt = c.kt0; kt < c.kt1; ++kt) {
-        // A K block's combined scale, as the reference forms it: sa * sb in fp32.
-        const float scale = sa_next * sb_next;
-        if (kt + 1 < c.kt1) {
-          if (row_ok) sa_next = __ldg(sap + int64_t(kt + 1) * p.sa_k);
-          if (cols_ok) sb_next = __ldg(sbp + int64_t(kt + 1) * p.sb_k);
-        }
-        ok = mbar_wait(acc_full(acc), acc_phase, abort_flag, kWaitAccFull) && ok;
-        tc_fence_after();
-        if (warp_rows && cols_ok) {
-          const uint32_t t = t_lane + uint32_t(acc * BN + g * COLS);
+      for (int kt_base = c.kt0; kt_base < c.kt1; kt_base += PF) {
 #pragma unroll
-          for (int ch = 0; ch < COLS / 32; ++ch) {
-            float part[32];
-            tmem_ld32(t + 32 * ch, part);
+        for (int j = 0; j < PF; ++j) {
+          const int kt = kt_base + j;
+          if (kt < c.kt1) {
+            const float sa_v = pa[j], sb_v = pb[j];
+            float sa2_v = 0.f;
+            if constexpr (SWAP && BN > 32) sa2_v = pa2[j];
+            if (kt + PF < c.kt1) load_scales(kt + PF, j);
+            ok = mbar_wait(acc_full(acc), acc_phase, abort_flag, kWaitAccFull) && ok;
+            tc_fence_after();
+            if (work) {
+              const uint32_t t = t_lane + uint32_t(acc * BN + g * COLS);
+              if constexpr (!SWAP) {
+                // One scale per thread: sa[row] * sb[block], as the reference forms it.
+                const float scale = sa_v * sb_v;
 #pragma unroll
-            for (int j = 0; j < 32; ++j) accum[32 * ch + j] = fmaf(part[j], scale, accum[32 * ch + j]);
+                for (int ch = 0; ch < COLS / 32; ++ch) {
+                  float part[32];
+                  tmem_ld<32>(t + 32 * ch, part);
+#pragma unroll
+                  for (int i = 0; i < 32; ++i) accum[32 * ch + i] = fmaf(part[i], scale, accum[32 * ch + i]);
+                }
+              } else {
+                constexpr int CH = BN < 32 ? BN : 32;
+#pragma unroll
+                for (int ch = 0; ch < BN / CH; ++ch) {
+                  float part[CH];
+                  tmem_ld<CH>(t + CH * ch, part);
+                  const float src = ch == 0 ? sa_v : sa2_v;
+#pragma unroll
+                  for (int i = 0; i < CH; ++i) {
+                    const float scale = __shfl_sync(0xffffffffu, src, i) * sb_v;
+                    accum[CH * ch + i] = fmaf(part[i], scale, accum[CH * ch + i]);
+                  }
+                }
+              }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty(acc));
+            if (++acc == ACC_BUFS) {
+              acc = 0;
+              acc_phase ^= 1u;
+            }
           }
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(acc_empty(acc));
-        if (++acc == ACC_BUFS) {
-          acc = 0;
-          acc_phase ^= 1u;
         }
       }
 
-      bool store = warp_rows && cols_ok;
+      bool store = work;
       if (p.splits > 1) {
         // Deterministic split-K: publish this split's partial, count arrivals;
         // the last CTA of the tile sums all partials in split order.
-        float* ws_tile = p.workspace + int64_t(c.tile) * (128 * BN) + row * BN + g * COLS;
         const int64_t split_stride = int64_t(p.tiles) * (128 * BN);
+        float* ws_tile = p.workspace + int64_t(c.tile) * (128 * BN);
         if (row_ok && cols_ok && ok) {
+          if constexpr (!SWAP) {
+            float* w = ws_tile + c.split * split_stride + row * BN + g * COLS;
 #pragma unroll
-          for (int j = 0; j < COLS; j += 4)
-            __stcg(reinterpret_cast<float4*>(ws_tile + c.split * split_stride + j),
-                   make_float4(accum[j], accum[j + 1], accum[j + 2], accum[j + 3]));
+            for (int j = 0; j < COLS; j += 4)
+              __stcg(reinterpret_cast<float4*>(w + j),
+                     make_float4(accum[j], accum[j + 1], accum[j + 2], accum[j + 3]));
+          } else {
+            float* w = ws_tile + c.split * split_stride + row;
+#pragma unroll
+            for (int j = 0; j < COLS; ++j) __stcg(w + j * 128, accum[j]);
+          }
         }
         __threadfence();
         named_bar_sync(1, Cfg::EPI_THREADS);
@@ -324,22 +437,34 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
         if (last) {
           __threadfence();
           if (row_ok && cols_ok) {
+            if constexpr (!SWAP) {
+              const float* w = ws_tile + row * BN + g * COLS;
 #pragma unroll
-            for (int j = 0; j < COLS; j += 4) {
-              float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-              for (int s = 0; s < p.splits; ++s) {
-                const float4 t = s == c.split
-                                     ? make_float4(accum[j], accum[j + 1], accum[j + 2], accum[j + 3])
-                                     : __ldcg(reinterpret_cast<const float4*>(ws_tile + s * split_stride + j));
-                x.x += t.x;
-                x.y += t.y;
-                x.z += t.z;
-                x.w += t.w;
+              for (int j = 0; j < COLS; j += 4) {
+                float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int s = 0; s < p.splits; ++s) {
+                  const float4 t = s == c.split
+                                       ? make_float4(accum[j], accum[j + 1], accum[j + 2], accum[j + 3])
+                                       : __ldcg(reinterpret_cast<const float4*>(w + s * split_stride + j));
+                  x.x += t.x;
+                  x.y += t.y;
+                  x.z += t.z;
+                  x.w += t.w;
+                }
+                accum[j] = x.x;
+                accum[j + 1] = x.y;
+                accum[j + 2] = x.z;
+                accum[j + 3] = x.w;
               }
-              accum[j] = x.x;
-              accum[j + 1] = x.y;
-              accum[j + 2] = x.z;
-              accum[j + 3] = x.w;
+            } else {
+              const float* w = ws_tile + row;
+#pragma unroll
+              for (int j = 0; j < COLS; ++j) {
+                float x = 0.f;
+                for (int s = 0; s < p.splits; ++s)
+                  x += s == c.split ? accum[j] : __ldcg(w + s * split_stride + j * 128);
+                accum[j] = x;
+              }
             }
           }
           if (ew == 0 && lane == 0) p.counters[c.tile] = 0;  // ready for the next launch
@@ -347,33 +472,42 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
       }
 
       if (store && ok) {
-        // bf16 rows -> 128B-swizzled [32 x 64] staging tile -> TMA store.
+        if constexpr (!SWAP) {
+          // bf16 rows -> [32 x 32] chunks, 64-byte swizzle, two buffers in
+          // turn so one chunk's TMA store overlaps the next chunk's writes.
 #pragma unroll
-        for (int ch = 0; ch < COLS / 64; ++ch) {
-          if (col0 + 64 * ch >= p.N) break;
-          if (lane == 0) bulk_wait_read0();  // the previous store has read the buffer
+          for (int ch = 0; ch < COLS / 32; ++ch) {
+            if (col0 + 32 * ch >= p.N) break;
+            const uint32_t buf = out_buf + uint32_t(out_chunk) * 2048u;
+            if (lane == 0) bulk_wait_read1();  // the store that last read this buffer is done
+            __syncwarp();
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              const float* a = accum + 32 * ch + 8 * v;
+              const uint32_t dst = buf + uint32_t(lane) * 64u + uint32_t((v ^ ((lane >> 1) & 3)) * 16);
+              st_shared_v4(dst, bf16x2_bits(a[0], a[1]), bf16x2_bits(a[2], a[3]), bf16x2_bits(a[4], a[5]),
+                           bf16x2_bits(a[6], a[7]));
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&p.map_c, col0 + 32 * ch, c.tr * 128 + 32 * quarter, buf);
+              bulk_commit();
+            }
+            out_chunk ^= 1;
+          }
+        } else {
+          // [BN tokens x 32 weight rows] bf16, row-major: TMA box {32, BN}.
+          if (lane == 0) bulk_wait_read0();
           __syncwarp();
 #pragma unroll
-          for (int v = 0; v < 8; ++v) {
-            const float* a = accum + 64 * ch + 8 * v;
-            __nv_bfloat162 b0 = __floats2bfloat162_rn(a[0], a[1]);
-            __nv_bfloat162 b1 = __floats2bfloat162_rn(a[2], a[3]);
-            __nv_bfloat162 b2 = __floats2bfloat162_rn(a[4], a[5]);
-            __nv_bfloat162 b3 = __floats2bfloat162_rn(a[6], a[7]);
-            uint4 w;
-            w.x = *reinterpret_cast<uint32_t*>(&b0);
-            w.y = *reinterpret_cast<uint32_t*>(&b1);
-            w.z = *reinterpret_cast<uint32_t*>(&b2);
-            w.w = *reinterpret_cast<uint32_t*>(&b3);
-            const uint32_t dst = out_buf + uint32_t(lane) * 128u + uint32_t((v ^ (lane & 7)) * 16);
-            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(w.x), "r"(w.y),
-                         "r"(w.z), "r"(w.w)
-                         : "memory");
-          }
+          for (int j = 0; j < COLS; ++j)
+            st_shared_b16(out_buf + uint32_t(j) * 64u + uint32_t(lane) * 2u,
+                          __bfloat16_as_ushort(__float2bfloat16_rn(accum[j])));
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&p.map_c, col0 + 64 * ch, c.tm * 128 + 32 * quarter, out_buf);
+            tma_store_2d(&p.map_c, c.tr * 128 + 32 * quarter, c.tc * BN, out_buf);
             bulk_commit();
           }
         }

@@ -1,0 +1,195 @@
+"""CPU tests of the drop-in boundary: argument validation (the reference's
+tests/test_validation.py restated), the C ABI library (loads, exports every
+symbol include/blockfp8_b200.h declares, planner and sizing answers), the
+torch op schemas, and the public torch helpers against the golden vectors."""
+
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+import torch
+
+import blockfp8
+import blockfp8_b200
+from blockfp8_b200 import _native
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+GOLDEN = os.path.join(ROOT, "tests", "golden")
+FP8 = torch.float8_e4m3fn
+
+
+# ---- validation ----------------------------------------------------------------
+
+def _args(m=4, n=256, k=512, col_major=True):
+    a_q = torch.zeros(m, k).to(FP8)
+    b_q = torch.zeros(n, k).to(FP8)
+    kb, nb = -(-k // 128), -(-n // 128)
+    a_s = torch.ones(kb, m).t() if col_major else torch.ones(m, kb)
+    return a_q, a_s, b_q, torch.ones(nb, kb)
+
+
+@pytest.mark.parametrize("col_major", [True, False])
+def test_valid_args(col_major):
+    assert blockfp8.check_gemm_args(*_args(col_major=col_major), torch.bfloat16) == (4, 256, 512)
+
+
+def test_tails_are_accepted():
+    assert blockfp8.check_gemm_args(*_args(m=3, n=136, k=144), torch.bfloat16) == (3, 136, 144)
+
+
+@pytest.mark.parametrize("mutate, match", [
+    (lambda a: (a[0].float(), *a[1:]), "float8_e4m3fn"),
+    (lambda a: (a[0][:, :500], a[1], a[2], a[3]), "K mismatch"),
+    (lambda a: (a[0], a[1], a[2].to(torch.float8_e5m2), a[3]), "float8_e4m3fn"),
+    (lambda a: (a[0], a[1].double(), a[2], a[3]), "a_scales"),
+    (lambda a: (a[0], a[1][:, :3], a[2], a[3]), "a_scales"),
+    (lambda a: (a[0], a[1], a[2], a[3][:1]), "b_scales"),
+    (lambda a: (a[0].t().contiguous().t(), *a[1:]), "row-major"),
+])
+def test_rejects(mutate, match):
+    with pytest.raises(ValueError, match=match):
+        blockfp8.check_gemm_args(*mutate(_args()), torch.bfloat16)
+
+
+def test_rejects_unaligned_k_and_n():
+    with pytest.raises(ValueError, match="K must be"):
+        blockfp8.check_gemm_args(*_args(k=200), torch.bfloat16)
+    with pytest.raises(ValueError, match="N must be"):
+        blockfp8.check_gemm_args(*_args(n=100), torch.bfloat16)
+
+
+def test_rejects_other_output_dtypes():
+    with pytest.raises(ValueError, match="out_dtype"):
+        blockfp8.check_gemm_args(*_args(), torch.float16)
+
+
+def test_cpu_tensors_point_to_the_reference():
+    with pytest.raises(ValueError, match="reference_gemm"):
+        blockfp8.gemm(*_args())
+
+
+def test_bf16_entry_points_reject_cpu_and_bad_layouts():
+    b_q, b_s = _args()[2:]
+    with pytest.raises(ValueError):
+        blockfp8.linear(torch.zeros(2, 512, dtype=torch.bfloat16), b_q, b_s)  # CPU tensor
+    with pytest.raises(ValueError):
+        blockfp8.gemm_bf16(torch.zeros(2, 512), b_q, b_s)  # float32
+    with pytest.raises(ValueError, match="CUDA"):
+        blockfp8.gemm_bf16(torch.zeros(2, 512, dtype=torch.bfloat16), b_q, b_s)
+
+
+# ---- the API surface -------------------------------------------------------------
+
+def test_public_names_match_the_reference_api():
+    expected = {"BLOCK_N", "FP8_DTYPE", "FP8_MAX", "GROUP_K", "check_gemm_args", "configs",
+                "dequantize_activations", "dequantize_weights", "error_bound", "fused_configs",
+                "gemm", "gemm_bf16", "linear", "native_available", "prefers_fused",
+                "quantize_activations", "quantize_cuda", "quantize_weights", "reference_gemm"}
+    assert expected <= set(blockfp8.__all__)
+    for name in expected:
+        assert getattr(blockfp8, name) is getattr(blockfp8_b200, name)
+    from blockfp8.reference import BF16_U  # submodule aliases exist
+    assert BF16_U == 2.0 ** -8
+
+
+def test_torch_helpers_match_the_reference_vectors():
+    """quantize_activations / quantize_weights / reference_gemm of the public
+    API give the reference's bits (they prepare operands; not the hot path)."""
+    g = np.load(os.path.join(GOLDEN, "quant.npz"))
+    for i in range(int(g["act_count"])):
+        x = torch.from_numpy(g[f"act{i}_x_bf16"].view(np.int16)).view(torch.bfloat16)
+        for j, eps in enumerate(g["act_eps"]):
+            q, s = blockfp8.quantize_activations(x, eps=float(eps))
+            assert np.array_equal(q.view(torch.uint8).numpy(), g[f"act{i}_eps{j}_q"])
+            assert np.array_equal(s.numpy(), g[f"act{i}_eps{j}_s"]) and s.stride() == (1, x.shape[0])
+    for i in range(int(g["wgt_count"])):
+        q, s = blockfp8.quantize_weights(torch.from_numpy(g[f"wgt{i}_w"]))
+        assert np.array_equal(q.view(torch.uint8).numpy(), g[f"wgt{i}_q"])
+        assert np.array_equal(s.numpy(), g[f"wgt{i}_s"])
+    gm = np.load(os.path.join(GOLDEN, "gemm.npz"))
+    for i in range(int(gm["g_count"])):
+        args = [torch.from_numpy(gm[f"g{i}_a"]).view(FP8), torch.from_numpy(gm[f"g{i}_sa"]),
+                torch.from_numpy(gm[f"g{i}_b"]).view(FP8), torch.from_numpy(gm[f"g{i}_sb"])]
+        assert np.array_equal(blockfp8.reference_gemm(*args).numpy(), gm[f"g{i}_c"])
+
+
+# ---- the C ABI library ------------------------------------------------------------
+
+def _declared_functions():
+    header = open(os.path.join(ROOT, "include", "blockfp8_b200.h")).read()
+    header = re.sub(r"/\*.*?\*/", "", header, flags=re.S)
+    return sorted(set(re.findall(r"\b(bfp8_[a-z_0-9]+)\s*\(", header)))
+
+
+def test_c_abi_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(_native.CAPI_LIB)
+    names = _declared_functions()
+    assert len(names) >= 14
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+    assert set(names) == set(_native._SIGNATURES), "ctypes signatures out of date with the header"
+
+
+def test_c_abi_answers_without_a_gpu():
+    lib = _native.capi()
+    assert lib.bfp8_abi_version() == 1
+    n = lib.bfp8_num_configs()
+    assert n >= 1 and lib.bfp8_num_fused_configs() >= 1
+    names = [lib.bfp8_config_name(i).decode() for i in range(n)]
+    assert names == blockfp8.configs()
+    assert lib.bfp8_config_name(n) is None
+    for m, nn, k in [(1, 6144, 4096), (16, 24576, 4096), (256, 6144, 4096), (8192, 24576, 4096),
+                     (3000, 4096, 12288), (33, 264, 272)]:
+        plan = lib.bfp8_choose_plan(m, nn, k, 148)
+        assert 0 <= plan.config < n and plan.splits >= 1 and plan.fused == 0
+        fplan = lib.bfp8_choose_fused_plan(m, nn, k, 148)
+        assert fplan.fused == 1
+        p = _native.GemmProblem(M=m, N=nn, K=k)
+        tiles, kt = ctypes.c_int(), ctypes.c_int()
+        assert lib.bfp8_plan_shape(ctypes.byref(p), plan, ctypes.byref(tiles), ctypes.byref(kt)) == 0
+        assert kt.value == -(-k // 128)
+        ws = lib.bfp8_workspace_bytes(ctypes.byref(p), plan)
+        cnt = lib.bfp8_counters_needed(ctypes.byref(p), plan)
+        splits = -(-kt.value // -(-kt.value // min(plan.splits, kt.value)))
+        assert (ws == 0) == (splits == 1) and (cnt == 0) == (splits == 1)
+        assert lib.bfp8_workspace_bytes(ctypes.byref(p), fplan) >= m * k  # quantized x lives there
+    bad = _native.Plan(99, 1, 0)
+    p = _native.GemmProblem(M=1, N=128, K=128)
+    assert lib.bfp8_workspace_bytes(ctypes.byref(p), bad) < 0
+    assert "config" in lib.bfp8_last_error().decode()
+
+
+def test_c_abi_rejects_bad_problems_without_launching():
+    lib = _native.capi()
+    p = _native.GemmProblem(M=4, N=256, K=200)  # K % 16 != 0
+    assert lib.bfp8_launch_gemm(ctypes.byref(p), _native.Plan(0, 1, 0), None, None, None) == -1
+    assert "K must be" in lib.bfp8_last_error().decode()
+    q = _native.QuantProblem(M=4, K=12)
+    assert lib.bfp8_launch_quantize(ctypes.byref(q), None) == -1
+
+
+def test_torch_op_schemas_are_the_reference_ones():
+    schemas = {s.name: str(s) for s in torch._C._jit_get_all_schemas() if s.name.startswith("blockfp8::")}
+    assert "blockfp8::gemm(Tensor a, Tensor a_scales, Tensor b, Tensor b_scales, int config=-1, " \
+           "int split_k=0) -> Tensor" in schemas.values()
+    assert "blockfp8::gemm_bf16(Tensor x, Tensor b, Tensor b_scales, int config=-1, " \
+           "int split_k=0, float eps=1e-10) -> Tensor" in schemas.values()
+    assert "blockfp8::quantize(Tensor x, float eps=1e-10) -> (Tensor, Tensor)" in schemas.values()
+    assert "blockfp8::linear(Tensor x, Tensor b, Tensor b_scales) -> Tensor" in schemas.values()
+    assert "blockfp8::prefers_fused(int m, int n, int k) -> bool" in schemas.values()
+    assert torch.ops.blockfp8.config_names().split(";") == blockfp8.configs()
+    assert isinstance(torch.ops.blockfp8.prefers_fused(1, 6144, 4096), bool)
+
+
+def test_fake_kernels_give_the_output_layouts():
+    from torch._subclasses.fake_tensor import FakeTensorMode
+    with FakeTensorMode():
+        x = torch.empty(5, 256, dtype=torch.bfloat16)
+        b = torch.empty(128, 256, dtype=FP8)
+        sb = torch.empty(1, 2)
+        q, s = torch.ops.blockfp8.quantize(x, 1e-10)
+        assert q.shape == (5, 256) and q.dtype == FP8 and s.shape == (5, 2) and s.stride() == (1, 5)
+        assert torch.ops.blockfp8.linear(x, b, sb).shape == (5, 128)
+        assert torch.ops.blockfp8.gemm_bf16(x, b, sb, -1, 0, 1e-10).dtype == torch.bfloat16
