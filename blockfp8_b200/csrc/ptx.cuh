@@ -56,12 +56,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking test of the same condition (no suspend).
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait until the phase with the given parity has completed.  Returns false
 // if the wait gave up: on a timeout, or at once when another warp has raised
 // *abort.  abort == nullptr: a drain wait that only the timeout ends.
 // `where` identifies the wait site in the status code.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
                                           uint32_t where) {
+  if (mbar_test_wait(bar, parity)) return true;  // already complete: the common case
 #pragma unroll 1
   for (int i = 0; i < 256; ++i)
     if (mbar_try_wait(bar, parity)) return true;
