@@ -69,6 +69,7 @@ _SIGNATURES = {
     "bfp8_counters_needed": ([ctypes.POINTER(GemmProblem), Plan], ctypes.c_int),
     "bfp8_launch_gemm": ([ctypes.POINTER(GemmProblem), Plan, ctypes.c_void_p, ctypes.c_void_p,
                           ctypes.c_void_p], ctypes.c_int),
+    "bfp8_launch_gemm_noalloc": ([ctypes.POINTER(GemmProblem), Plan, ctypes.c_void_p], ctypes.c_int),
     "bfp8_launch_quantize": ([ctypes.POINTER(QuantProblem), ctypes.c_void_p], ctypes.c_int),
     "bfp8_device_status": ([ctypes.c_int], ctypes.c_int64),
 }

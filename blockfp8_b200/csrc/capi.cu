@@ -316,6 +316,31 @@ int launch_quant(const QuantParams& qp, cudaStream_t stream, int num_sms) {
   return BFP8_OK;
 }
 
+// ---- fixed scratch for callers that cannot allocate --------------------------
+// One array per device that loads this library, held until the process
+// exits: the first BFP8_STATIC_COUNTER_BYTES hold split-K arrival counters,
+// the rest the workspace (split-K partials, the fused path's quantized
+// activations).  Host code must not use the array's name as a device
+// address; static_scratch() looks the address up per device.
+static __device__ __align__(256) unsigned char g_static_scratch[BFP8_STATIC_SCRATCH_BYTES];
+
+// Device address of g_static_scratch on the current device, looked up once
+// per device (cudaGetSymbolAddress, with that device current) and cached.
+int static_scratch(int dev, unsigned char** out) {
+  static std::mutex mu;
+  static unsigned char* ptrs[kMaxDevices] = {};
+  if (dev < 0 || dev >= kMaxDevices) return fail(BFP8_EINVAL, "device index out of range");
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptrs[dev]) {
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_static_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(static scratch)");
+    ptrs[dev] = static_cast<unsigned char*>(ptr);
+  }
+  *out = ptrs[dev];
+  return BFP8_OK;
+}
+
 }  // namespace
 }  // namespace bfp8
 
@@ -485,6 +510,36 @@ int bfp8_launch_gemm(const bfp8_gemm_problem* pp, bfp8_plan plan, float* workspa
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return cuda_fail(err, "GEMM kernel launch");
   return BFP8_OK;
+}
+
+int bfp8_launch_gemm_noalloc(const bfp8_gemm_problem* p, bfp8_plan plan, void* stream) {
+  if (!p) return fail(BFP8_EINVAL, "null problem");
+  if (!config_ok(plan.config)) return fail(BFP8_EINVAL, "config out of range");
+  if (plan.splits < 1) return fail(BFP8_EINVAL, "splits must be >= 1");
+  if (p->M <= 0) return bfp8_launch_gemm(p, plan, nullptr, nullptr, stream);
+  const int64_t ws = bfp8_workspace_bytes(p, plan);
+  const int counters = bfp8_counters_needed(p, plan);
+  if (ws < 0 || counters < 0) return int(ws < 0 ? ws : counters);
+  const int64_t ws_room = int64_t(BFP8_STATIC_SCRATCH_BYTES) - BFP8_STATIC_COUNTER_BYTES;
+  if (ws > ws_room || int64_t(counters) * 4 > BFP8_STATIC_COUNTER_BYTES)
+    return fail(BFP8_EINVAL, "this plan needs " + std::to_string(ws) + " bytes of workspace and " +
+                                 std::to_string(counters) + " counters; the fixed scratch holds " +
+                                 std::to_string(ws_room) + " bytes and " +
+                                 std::to_string(BFP8_STATIC_COUNTER_BYTES / 4) +
+                                 " counters (use fewer splits, or bfp8_launch_gemm with a workspace)");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  unsigned char* base = nullptr;
+  if (int r = static_scratch(dev, &base)) return r;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // The array keeps the previous call's contents; counters must start at zero.
+  if (counters > 0) {
+    e = cudaMemsetAsync(base, 0, size_t(counters) * 4, s);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(static scratch counters)");
+  }
+  return bfp8_launch_gemm(p, plan, ws ? reinterpret_cast<float*>(base + BFP8_STATIC_COUNTER_BYTES) : nullptr,
+                          counters ? reinterpret_cast<int*>(base) : nullptr, stream);
 }
 
 int64_t bfp8_device_status(int reset) {

@@ -110,6 +110,28 @@ int bfp8_counters_needed(const bfp8_gemm_problem* p, bfp8_plan plan);
 int bfp8_launch_gemm(const bfp8_gemm_problem* p, bfp8_plan plan, float* workspace, int* counters,
                      void* stream);
 
+/* The same launch without any caller-provided or allocated device memory.
+ * No counterpart in the reference.  For callers that cannot allocate device
+ * memory on this path -- a serving loop whose device memory is all reserved
+ * up front, a host runtime bound through FFI without a CUDA allocator, code
+ * that must not risk cudaMalloc's implicit device synchronisation -- the
+ * split-K partials, the split-K counters and the fused path's quantized
+ * activations live in one fixed array in the library's device memory,
+ * BFP8_STATIC_SCRATCH_BYTES per device, held by every GPU that loads the
+ * library until the process exits.  A plan that needs more than it holds
+ * (bfp8_workspace_bytes() above BFP8_STATIC_SCRATCH_BYTES -
+ * BFP8_STATIC_COUNTER_BYTES, or more than BFP8_STATIC_COUNTER_BYTES / 4
+ * counters) is rejected with BFP8_EINVAL and nothing is launched.  The first
+ * call on a device looks the array's address up (cudaGetSymbolAddress), so
+ * make it before any stream capture.  Each call clears the counters it uses
+ * (cudaMemsetAsync on the stream); every call shares the one array, so calls
+ * that overlap on the GPU (other streams, other host threads) race and must
+ * be serialised by the caller.  Allocates nothing.  Same results as
+ * bfp8_launch_gemm under the same plan. */
+#define BFP8_STATIC_SCRATCH_BYTES (16u << 20)
+#define BFP8_STATIC_COUNTER_BYTES (64u << 10)
+int bfp8_launch_gemm_noalloc(const bfp8_gemm_problem* p, bfp8_plan plan, void* stream);
+
 /* Launch the activation quantizer; replaces launch_quantize
  * (csrc/blockfp8.h:76).  Returns BFP8_OK, BFP8_EINVAL or BFP8_ECUDA. */
 int bfp8_launch_quantize(const bfp8_quant_problem* p, void* stream);
