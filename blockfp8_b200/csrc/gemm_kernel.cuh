@@ -261,6 +261,11 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_e4m3_f32(128, BN);
+      // Descriptors of stage 0's tiles; a stage or a K step only moves the
+      // 14-bit start-address field (16-byte units), which never carries out
+      // (shared memory ends below 256 KB).
+      const uint64_t desc_a0 = smem_desc_k128_sw128(s_tiles);
+      const uint64_t desc_b0 = smem_desc_k128_sw128(s_tiles + Cfg::A_BYTES);
       int stage = 0, acc = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
@@ -273,13 +278,11 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = s_tiles + uint32_t(stage) * Cfg::STAGE_BYTES;
-          const uint32_t b_addr = a_addr + Cfg::A_BYTES;
+          const uint64_t stage_off = uint64_t(stage) * (Cfg::STAGE_BYTES >> 4);
           const uint32_t d = tmem_base + uint32_t(acc * BN);
 #pragma unroll
-          for (int k = 0; k < 4; ++k)
-            mma_f8(d, smem_desc_k128_sw128(a_addr + 32 * k), smem_desc_k128_sw128(b_addr + 32 * k),
-                   idesc, k > 0 ? 1u : 0u);
+          for (int k = 0; k < 4; ++k)  // K step of 32 e4m3 = 32 bytes = 2 descriptor units
+            mma_f8(d, desc_a0 + stage_off + 2 * k, desc_b0 + stage_off + 2 * k, idesc, k > 0 ? 1u : 0u);
           mma_commit(empty(stage));   // the smem stage is free once these MMAs are done
           mma_commit(acc_full(acc));  // ... and the partial sums are in TMEM
           if (++stage == STAGES) {
