@@ -5,11 +5,12 @@
 // One persistent, warp-specialised CTA per SM walks a static list of work
 // units (an output tile and a range of 128-wide K blocks):
 //
-//   warp 0      TMA producer: the two operand tiles of each K block
-//               (128-byte swizzle, 128 bytes = one K block per row) into a
-//               STAGES-deep shared-memory ring; completion is counted in
-//               bytes on the stage's "full" mbarrier;
-//   warp 1      MMA issuer (one thread): per K block, four
+//   warps 0, 3  TMA producers (one thread each, alternate K blocks): the
+//               two operand tiles of each K block (128-byte swizzle, 128
+//               bytes = one K block per row) into a STAGES-deep
+//               shared-memory ring; completion is counted in bytes on the
+//               stage's "full" mbarrier;
+//   warps 1, 2  MMA issuers (one thread each, alternate K blocks): four
 //               tcgen05.mma.kind::f8f6f4 (K = 32 each, e4m3 x e4m3 -> f32)
 //               into one of ACC_BUFS tensor-memory (TMEM) partial buffers,
 //               the first with the accumulator input disabled, so the buffer
@@ -81,8 +82,9 @@ struct GemmCfg {
   static constexpr int EPI_WG = SWAP ? 1 : BN / COLS;
   static constexpr int EPI_WARPS = 4 * EPI_WG;
   static constexpr int EPI_THREADS = 32 * EPI_WARPS;
-  // Warpgroup 0: warp 0 TMA, warp 1 MMA, warps 2-3 idle; warpgroups 1.. the
-  // epilogue, so registers can move between the roles by warpgroup.
+  // Warpgroup 0: TMA producers (warps 0, 3) and MMA issuers (warps 1, 2);
+  // warpgroups 1.. the epilogue, so registers can move between the roles by
+  // warpgroup.
   static constexpr int THREADS = 128 + EPI_THREADS;
   // Register split (setmaxnreg) when the launch share is too small for the
   // epilogue's 128 accumulators: warpgroup 0 gives up all but REG_LOW.
@@ -106,7 +108,8 @@ struct GemmCfg {
   static constexpr int SMEM_TILES = STAGES * STAGE_BYTES;
   static constexpr int SMEM_OUT = ((EPI_WARPS * OUT_BYTES + 1023) / 1024) * 1024;
   static constexpr int NUM_BARS = 2 * STAGES + 2 * ACC_BUFS + 1;
-  static constexpr int SMEM_BYTES = 1024 + SMEM_TILES + SMEM_OUT + NUM_BARS * 8 + 16;
+  static constexpr int SMEM_MISC = 16 + 4 * STAGES;  // TMEM slot, flags, last load per stage
+  static constexpr int SMEM_BYTES = 1024 + SMEM_TILES + SMEM_OUT + NUM_BARS * 8 + SMEM_MISC;
   static_assert(SMEM_BYTES <= 232448, "more shared memory than one sm_100 CTA can have");
   static_assert(TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM allocation");
   static_assert(STAGE_BYTES % 1024 == 0, "stages must stay 1024-byte aligned");
@@ -180,6 +183,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
   uint32_t* misc = reinterpret_cast<uint32_t*>(smem + Cfg::SMEM_TILES + Cfg::SMEM_OUT + 8 * Cfg::NUM_BARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 1);
   volatile int* last_flag = reinterpret_cast<volatile int*>(misc + 2);
+  volatile int* stage_seq = reinterpret_cast<volatile int*>(misc + 4);  // last K block loaded per stage
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -192,8 +196,9 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
       mbar_init(acc_full(a), 1);
       mbar_init(acc_empty(a), Cfg::EPI_WARPS);
     }
-    mbar_init(mma_done, 1);
+    mbar_init(mma_done, 2);  // one commit from each MMA issuer
     *abort_flag = 0;
+    for (int st = 0; st < STAGES; ++st) stage_seq[st] = -1;
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -212,95 +217,91 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
 
   if (warp < 4) {
     if constexpr (Cfg::SPLIT_REGS) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(Cfg::REG_LOW));
-  if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
+    // Two TMA producers (warps 0 and 3) and two MMA issuers (warps 1 and 2),
+    // one thread each, take alternate K blocks of the CTA's sequence: the
+    // per-K-block cost of the barrier tests and instruction issue is paid by
+    // two threads in parallel.  K block i of the sequence always uses smem
+    // stage i % STAGES (phase (i / STAGES) & 1) and TMEM buffer i % ACC_BUFS
+    // (phase (i / ACC_BUFS) & 1), whoever handles it.
+    const bool producer = warp == 0 || warp == 3;
+    const int role = (warp == 0 || warp == 1) ? 0 : 1;  // which half of the K blocks
     if (lane == 0) {
-      // Activations are re-read by many tiles: keep them; weights streamed
-      // once (decode) go first.
-      const uint64_t pol_act = policy_evict_last();
-      const uint64_t pol_wgt = p.stream_b ? policy_evict_first() : policy_evict_normal();
-      const uint64_t pol_a = SWAP ? pol_wgt : pol_act;
-      const uint64_t pol_b = SWAP ? pol_act : pol_wgt;
-      int stage = 0;
-      uint32_t phase = 0;
-      int issued = 0;
-      bool ok = true;
-      for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
-        const UnitCoord c = unit_coord(p, u);
-        for (int kt = c.kt0; kt < c.kt1; ++kt) {
-          if (!mbar_wait(empty(stage), phase ^ 1u, abort_flag, kWaitEmpty)) {
-            ok = false;
-            break;
-          }
-          const uint32_t dst = s_tiles + uint32_t(stage) * Cfg::STAGE_BYTES;
-          mbar_arrive_expect_tx(full(stage), Cfg::STAGE_BYTES);
-          tma_load_2d(dst, &p.map_a, kt * 128, c.tr * 128, full(stage), pol_a);
-          tma_load_2d(dst + Cfg::A_BYTES, &p.map_b, kt * 128, c.tc * BN, full(stage), pol_b);
-          ++issued;
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
+      if (producer) {
+        // ------------------------------------------------------------ TMA producer
+        // Activations are re-read by many tiles: keep them; weights streamed
+        // once (decode) go first.
+        const uint64_t pol_act = policy_evict_last();
+        const uint64_t pol_wgt = p.stream_b ? policy_evict_first() : policy_evict_normal();
+        const uint64_t pol_a = SWAP ? pol_wgt : pol_act;
+        const uint64_t pol_b = SWAP ? pol_act : pol_wgt;
+        int seq = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
+          const UnitCoord c = unit_coord(p, u);
+          for (int kt = c.kt0; kt < c.kt1; ++kt, ++seq) {
+            if ((seq & 1) != role) continue;
+            const int stage = seq % STAGES;
+            const uint32_t phase = uint32_t(seq / STAGES) & 1u;
+            if (!mbar_wait(empty(stage), phase ^ 1u, abort_flag, kWaitEmpty)) {
+              ok = false;
+              break;
+            }
+            const uint32_t dst = s_tiles + uint32_t(stage) * Cfg::STAGE_BYTES;
+            mbar_arrive_expect_tx(full(stage), Cfg::STAGE_BYTES);
+            tma_load_2d(dst, &p.map_a, kt * 128, c.tr * 128, full(stage), pol_a);
+            tma_load_2d(dst + Cfg::A_BYTES, &p.map_b, kt * 128, c.tc * BN, full(stage), pol_b);
+            stage_seq[stage] = seq;
           }
         }
-      }
-      // Every issued copy must land before the CTA exits (on the normal path
-      // the MMA thread has already seen them all).
-      const int pending = issued < STAGES ? issued : STAGES;
-      for (int i = 0; i < pending; ++i) {
-        if (stage == 0) {
-          stage = STAGES - 1;
-          phase ^= 1u;
-        } else {
-          --stage;
-        }
-        mbar_wait(full(stage), phase, nullptr, kWaitDrain);
-      }
-    }
-    __syncwarp();  // reconverge before the CTA-wide barrier (bar.sync is .aligned)
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_e4m3_f32(128, BN);
-      // Descriptors of stage 0's tiles; a stage or a K step only moves the
-      // 14-bit start-address field (16-byte units), which never carries out
-      // (shared memory ends below 256 KB).
-      const uint64_t desc_a0 = smem_desc_k128_sw128(s_tiles);
-      const uint64_t desc_b0 = smem_desc_k128_sw128(s_tiles + Cfg::A_BYTES);
-      int stage = 0, acc = 0;
-      uint32_t phase = 0, acc_phase = 0;
-      bool ok = true;
-      for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
-        const UnitCoord c = unit_coord(p, u);
-        for (int kt = c.kt0; kt < c.kt1; ++kt) {
-          if (!mbar_wait(acc_empty(acc), acc_phase ^ 1u, abort_flag, kWaitAccEmpty) ||
-              !mbar_wait(full(stage), phase, abort_flag, kWaitFull)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint64_t stage_off = uint64_t(stage) * (Cfg::STAGE_BYTES >> 4);
-          const uint32_t d = tmem_base + uint32_t(acc * BN);
+      } else {
+        // ------------------------------------------------------------ MMA issuer
+        constexpr uint32_t idesc = idesc_e4m3_f32(128, BN);
+        // Descriptors of stage 0's tiles; a stage or a K step only moves the
+        // 14-bit start-address field (16-byte units), which never carries out
+        // (shared memory ends below 256 KB).
+        const uint64_t desc_a0 = smem_desc_k128_sw128(s_tiles);
+        const uint64_t desc_b0 = smem_desc_k128_sw128(s_tiles + Cfg::A_BYTES);
+        int seq = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
+          const UnitCoord c = unit_coord(p, u);
+          for (int kt = c.kt0; kt < c.kt1; ++kt, ++seq) {
+            if ((seq & 1) != role) continue;
+            const int stage = seq % STAGES, acc = seq % ACC_BUFS;
+            const uint32_t phase = uint32_t(seq / STAGES) & 1u;
+            const uint32_t acc_phase = uint32_t(seq / ACC_BUFS) & 1u;
+            if (!mbar_wait(acc_empty(acc), acc_phase ^ 1u, abort_flag, kWaitAccEmpty) ||
+                !mbar_wait(full(stage), phase, abort_flag, kWaitFull)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint64_t stage_off = uint64_t(stage) * (Cfg::STAGE_BYTES >> 4);
+            const uint32_t d = tmem_base + uint32_t(acc * BN);
 #pragma unroll
-          for (int k = 0; k < 4; ++k)  // K step of 32 e4m3 = 32 bytes = 2 descriptor units
-            mma_f8(d, desc_a0 + stage_off + 2 * k, desc_b0 + stage_off + 2 * k, idesc, k > 0 ? 1u : 0u);
-          mma_commit(empty(stage));   // the smem stage is free once these MMAs are done
-          mma_commit(acc_full(acc));  // ... and the partial sums are in TMEM
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
-          if (++acc == ACC_BUFS) {
-            acc = 0;
-            acc_phase ^= 1u;
+            for (int k = 0; k < 4; ++k)  // K step of 32 e4m3 = 32 bytes = 2 descriptor units
+              mma_f8(d, desc_a0 + stage_off + 2 * k, desc_b0 + stage_off + 2 * k, idesc, k > 0 ? 1u : 0u);
+            mma_commit(empty(stage));   // the smem stage is free once these MMAs are done
+            mma_commit(acc_full(acc));  // ... and the partial sums are in TMEM
           }
         }
+        // All MMAs of both issuers complete before TMEM is freed.
+        mma_commit(mma_done);
+        mbar_wait(mma_done, 0, nullptr, kWaitMmaDone);
       }
-      // All MMAs of this thread complete before TMEM is freed.
-      mma_commit(mma_done);
-      mbar_wait(mma_done, 0, nullptr, kWaitMmaDone);
     }
-    __syncwarp();
-  }
+    __syncwarp();  // reconverge before the barriers below (bar.sync is .aligned)
+    if (producer) {
+      // Every issued copy must land before the CTA exits.  On the normal path
+      // the MMA threads have seen them all; after an abort, wait on the last
+      // load of each stage (its phase completes when its bytes arrive).
+      named_bar_sync(2, 64);  // both producers are done issuing
+      if (warp == 0 && lane == 0)
+        for (int st = 0; st < STAGES; ++st)
+          if (stage_seq[st] >= 0)
+            mbar_wait(full(st), uint32_t(stage_seq[st] / STAGES) & 1u, nullptr, kWaitDrain);
+      __syncwarp();
+    }
   } else {
     if constexpr (Cfg::SPLIT_REGS) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(Cfg::REG_HIGH));
     // ------------------------------------------------------------ promotion + epilogue
@@ -431,42 +432,40 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
             for (int j = 0; j < COLS; ++j) __stcg(w + j * 128, accum[j]);
           }
         }
-        __threadfence();
+        // Release: every epilogue thread's partial is ordered before the
+        // counter update by the barrier and lane 0's gpu-scope fence.
         named_bar_sync(1, Cfg::EPI_THREADS);
-        if (ew == 0 && lane == 0) *last_flag = atomicAdd(p.counters + c.tile, 1) == p.splits - 1;
+        if (ew == 0 && lane == 0) {
+          fence_acq_rel_gpu();
+          const bool is_last = atomicAdd(p.counters + c.tile, 1) == p.splits - 1;
+          if (is_last) fence_acq_rel_gpu();  // acquire: the other splits' partials
+          *last_flag = is_last;
+        }
         named_bar_sync(1, Cfg::EPI_THREADS);
         const bool last = *last_flag != 0;
         store = store && last;
         if (last) {
-          __threadfence();
           if (row_ok && cols_ok) {
-            if constexpr (!SWAP) {
-              const float* w = ws_tile + row * BN + g * COLS;
+            // Sum every split's partial (this CTA's own included, as written
+            // above) in split order starting from zero, like the reference:
+            // one pass per split with all of a split's loads in flight.
 #pragma unroll
-              for (int j = 0; j < COLS; j += 4) {
-                float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-                for (int s = 0; s < p.splits; ++s) {
-                  const float4 t = s == c.split
-                                       ? make_float4(accum[j], accum[j + 1], accum[j + 2], accum[j + 3])
-                                       : __ldcg(reinterpret_cast<const float4*>(w + s * split_stride + j));
-                  x.x += t.x;
-                  x.y += t.y;
-                  x.z += t.z;
-                  x.w += t.w;
+            for (int j = 0; j < COLS; ++j) accum[j] = 0.f;
+            for (int s = 0; s < p.splits; ++s) {
+              if constexpr (!SWAP) {
+                const float* w = ws_tile + s * split_stride + row * BN + g * COLS;
+#pragma unroll
+                for (int j = 0; j < COLS; j += 4) {
+                  const float4 t = __ldcg(reinterpret_cast<const float4*>(w + j));
+                  accum[j] += t.x;
+                  accum[j + 1] += t.y;
+                  accum[j + 2] += t.z;
+                  accum[j + 3] += t.w;
                 }
-                accum[j] = x.x;
-                accum[j + 1] = x.y;
-                accum[j + 2] = x.z;
-                accum[j + 3] = x.w;
-              }
-            } else {
-              const float* w = ws_tile + row;
+              } else {
+                const float* w = ws_tile + s * split_stride + row;
 #pragma unroll
-              for (int j = 0; j < COLS; ++j) {
-                float x = 0.f;
-                for (int s = 0; s < p.splits; ++s)
-                  x += s == c.split ? accum[j] : __ldcg(w + s * split_stride + j * 128);
-                accum[j] = x;
+                for (int j = 0; j < COLS; ++j) accum[j] += __ldcg(w + j * 128);
               }
             }
           }

@@ -168,6 +168,9 @@ __device__ __forceinline__ uint64_t policy_evict_normal() {
   return p;
 }
 
+// gpu-scope acquire-release fence (split-K counter hand-off).
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
 // ---- named barriers (a subset of the CTA's warps) ---------------------------------
 
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {
