@@ -123,43 +123,56 @@ def time_device(fn, reps, flush, warmup=3):
 
 
 class ClockSampler:
-    """nvidia-smi clock/throttle samples of this GPU during a timed region."""
+    """SM clock and throttle reasons of this GPU sampled every ~2 ms during a
+    timed region (NVML through nvidia_ml_py; nvidia-smi's 200 ms period is
+    longer than the region itself)."""
 
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "sw_power_cap": 0x4}
 
     def __init__(self, dev):
-        self.proc = None
+        import threading
+        self.samples = []
+        self.stop_flag = False
+        self.thread = None
         try:
+            import pynvml
+            pynvml.nvmlInit()
             uuid = str(torch.cuda.get_device_properties(dev).uuid)
             uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", uuid, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except Exception:
-            self.proc = None
+            self.nvml = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByUUID(uuid.encode())
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+            self.thread = threading.Thread(target=self._run, daemon=True)
+            self.thread.start()
+        except Exception as e:  # no NVML: report that instead of guessing
+            self.error = repr(e)
+
+    def _run(self):
+        n = self.nvml
+        while not self.stop_flag:
+            try:
+                mhz = n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM)
+                mask = n.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                power = n.nvmlDeviceGetPowerUsage(self.handle) / 1000.0
+                self.samples.append((mhz, mask, power))
+            except Exception:
+                pass
+            time.sleep(0.002)
 
     def stop(self):
-        if self.proc is None:
+        if self.thread is None:
+            return {"available": False, "error": getattr(self, "error", "")}
+        self.stop_flag = True
+        self.thread.join()
+        if not self.samples:
             return {"available": False}
-        self.proc.terminate()
-        try:
-            out, _ = self.proc.communicate(timeout=5)
-        except Exception:
-            self.proc.kill()
-            out = ""
-        rows = [r.split(",") for r in out.strip().splitlines() if r.count(",") >= 7]
-        if not rows:
-            return {"available": False}
-        sm = [float(r[0]) for r in rows]
-        mx = max(float(r[1]) for r in rows)
-        power = [float(r[2]) for r in rows]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[4 + i]})
-        loaded = [s for s, p in zip(sm, power) if p > 0.5 * max(power)] or sm
-        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": reasons,
-                "samples": len(rows), "power_w_max": max(power)}
+        sm = [s[0] for s in self.samples]
+        reasons = sorted({name for _, mask, _ in self.samples
+                          for name, bit in self.REASONS.items() if mask & bit})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(sm), "sm_mhz_min": min(sm), "power_w_max": max(s[2] for s in self.samples),
+                "source": "NVML every ~2 ms during the timed steps"}
 
 
 # ---- distributed plumbing --------------------------------------------------------
@@ -350,7 +363,6 @@ def main():
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     clocks = ClockSampler(dev) if rank == 0 else None
-    time.sleep(0.3 if clocks else 0)
     barrier(world)
     torch.cuda.synchronize()
     for i in range(args.steps):

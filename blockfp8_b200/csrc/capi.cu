@@ -52,7 +52,17 @@ struct ConfigEntry {
 
 template <class Cfg>
 void launch_cfg(const GemmParams& gp, int grid, cudaStream_t stream) {
-  gemm_kernel<Cfg><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(gp);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(Cfg::THREADS);
+  cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = gp.pdl ? 1 : 0;  // only right behind our own quantizer
+  cudaLaunchKernelEx(&cfg, gemm_kernel<Cfg>, gp);
 }
 
 template <class Cfg>
@@ -159,15 +169,6 @@ const TableEntry kPlanTable[] = {
 #include "plan_table.inc"
     {0, 0, 0, 0, 0}};
 constexpr int kPlanEntries = int(sizeof(kPlanTable) / sizeof(kPlanTable[0])) - 1;
-
-// Fused-path winners and whether each beat quantize-then-GEMM.
-struct FusedEntry {
-  int n, k, m, config, splits, wins;
-};
-const FusedEntry kFusedTable[] = {
-#include "fused_plan_table.inc"
-    {0, 0, 0, 0, 0, 0}};
-constexpr int kFusedEntries = int(sizeof(kFusedTable) / sizeof(kFusedTable[0])) - 1;
 
 // The entry for this (N, K) with the smallest tabulated M >= M, else the
 // largest (the reference's lookup rule, csrc/gemm_sm89.cu:158-169).
@@ -368,16 +369,19 @@ bfp8_plan bfp8_choose_plan(int M, int N, int K, int num_sms) {
   return heuristic_plan(M, N, K, num_sms, false);
 }
 
+// The fused path is the quantization kernel followed by the same GEMM
+// kernels, launched with programmatic dependent launch so the GEMM's
+// prologue and first weight loads overlap the quantizer; it takes the same
+// plan as the unfused GEMM.
 bfp8_plan bfp8_choose_fused_plan(int M, int N, int K, int num_sms) {
-  if (const FusedEntry* t = lookup(kFusedTable, kFusedEntries, M, N, K))
-    if (M <= t->m) return {t->config, t->splits, 1};
-  return heuristic_plan(M, N, K, num_sms, true);
+  bfp8_plan plan = bfp8_choose_plan(M, N, K, num_sms);
+  plan.fused = 1;
+  return plan;
 }
 
-int bfp8_prefers_fused(int M, int N, int K) {
-  const FusedEntry* t = lookup(kFusedTable, kFusedEntries, M, N, K);
-  return t && M <= t->m && t->wins ? 1 : 0;
-}
+// Quantize-then-GEMM in one call never loses to two separate launches (it
+// is the same two kernels, overlapped), so linear always takes it.
+int bfp8_prefers_fused(int M, int N, int K) { return M >= 0 && N > 0 && K > 0 ? 1 : 0; }
 
 int bfp8_plan_shape(const bfp8_gemm_problem* p, bfp8_plan plan, int* tiles, int* k_tiles) {
   if (!p || !config_ok(plan.config)) return fail(BFP8_EINVAL, "bad config id");
@@ -503,6 +507,7 @@ int bfp8_launch_gemm(const bfp8_gemm_problem* pp, bfp8_plan plan, float* workspa
   const int64_t a_bytes = int64_t(d.tiles_r) * 128 * p.K;
   gp.group_r = e.swap || a_bytes <= (int64_t(48) << 20) ? d.tiles_r : 8;
   gp.stream_b = (e.swap || p.M <= 128) ? 1 : 0;  // weights read once: evict them first
+  gp.pdl = fused ? 1 : 0;
 
   if (int r = ensure_smem_attr(plan.config, dev)) return r;
   const int grid = std::min(gp.units, sms);

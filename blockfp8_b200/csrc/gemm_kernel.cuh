@@ -70,6 +70,7 @@ struct GemmParams {
   int units;    // tiles * splits
   int group_r;  // raster: groups of group_r row tiles, rows fastest inside a group
   int stream_b;  // 1: weights are read once (decode): L2 evict-first for them
+  int pdl;       // 1: launched right behind our quantizer with programmatic dependent launch
 };
 
 template <int BN_, int STAGES_, bool SWAP_>
@@ -97,7 +98,9 @@ struct GemmCfg {
   static constexpr bool SPLIT_REGS = REGS_LAUNCH < 200;
   static_assert(!SPLIT_REGS || 128 * REG_LOW + EPI_THREADS * REG_HIGH <= REGS_LAUNCH * THREADS,
                 "register split exceeds the launch allocation");
-  static constexpr int ACC_BUFS = 512 / BN > 4 ? 4 : 512 / BN;
+  // TMEM partial buffers: as many as fit (up to 16), so for small tiles the
+  // MMAs can run far ahead of a unit's epilogue (split-K hand-off, store).
+  static constexpr int ACC_BUFS = 512 / BN > 16 ? 16 : 512 / BN;
   static constexpr int TMEM_COLS = ACC_BUFS * BN < 32 ? 32 : ACC_BUFS * BN;
   static constexpr int A_BYTES = BM * BK;
   static constexpr int B_BYTES = BN * BK;
@@ -234,6 +237,35 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
         const uint64_t pol_wgt = p.stream_b ? policy_evict_first() : policy_evict_normal();
         const uint64_t pol_a = SWAP ? pol_wgt : pol_act;
         const uint64_t pol_b = SWAP ? pol_act : pol_wgt;
+        // Weights are operand A when swapped, B otherwise.  After our own
+        // quantizer (p.pdl, programmatic dependent launch) the weight tiles
+        // of this thread's first K blocks (among the first STAGES) go out
+        // before griddepcontrol.wait, so they stream while the quantizer
+        // finishes; activation tiles only after it.
+        const CUtensorMap* map_w = SWAP ? &p.map_a : &p.map_b;
+        const CUtensorMap* map_x = SWAP ? &p.map_b : &p.map_a;
+        const uint32_t off_w = SWAP ? 0u : uint32_t(Cfg::A_BYTES);
+        const uint32_t off_x = SWAP ? uint32_t(Cfg::A_BYTES) : 0u;
+        const uint64_t pol_w = SWAP ? pol_a : pol_b;
+        const uint64_t pol_x = SWAP ? pol_b : pol_a;
+        auto w_row = [&](const UnitCoord& c) { return SWAP ? c.tr * 128 : c.tc * BN; };
+        auto x_row = [&](const UnitCoord& c) { return SWAP ? c.tc * BN : c.tr * 128; };
+        int early = 0;  // K blocks (of the whole sequence) whose weights went out early
+        if (p.pdl) {
+          int seq = 0;
+          for (int u = blockIdx.x; u < p.units && seq < STAGES; u += gridDim.x) {
+            const UnitCoord c = unit_coord(p, u);
+            for (int kt = c.kt0; kt < c.kt1 && seq < STAGES; ++kt, ++seq) {
+              if ((seq & 1) != role) continue;
+              const uint32_t dst = s_tiles + uint32_t(seq) * Cfg::STAGE_BYTES;  // stage = seq
+              mbar_arrive_expect_tx(full(seq), Cfg::STAGE_BYTES);
+              tma_load_2d(dst + off_w, map_w, kt * 128, w_row(c), full(seq), pol_w);
+              stage_seq[seq] = seq;
+            }
+          }
+          early = seq;
+        }
+        griddep_wait();  // activations are the previous kernel's output
         int seq = 0;
         bool ok = true;
         for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
@@ -241,15 +273,19 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
           for (int kt = c.kt0; kt < c.kt1; ++kt, ++seq) {
             if ((seq & 1) != role) continue;
             const int stage = seq % STAGES;
+            const uint32_t dst = s_tiles + uint32_t(stage) * Cfg::STAGE_BYTES;
+            if (seq < early) {  // weights already requested; add the activations
+              tma_load_2d(dst + off_x, map_x, kt * 128, x_row(c), full(stage), pol_x);
+              continue;
+            }
             const uint32_t phase = uint32_t(seq / STAGES) & 1u;
             if (!mbar_wait(empty(stage), phase ^ 1u, abort_flag, kWaitEmpty)) {
               ok = false;
               break;
             }
-            const uint32_t dst = s_tiles + uint32_t(stage) * Cfg::STAGE_BYTES;
             mbar_arrive_expect_tx(full(stage), Cfg::STAGE_BYTES);
-            tma_load_2d(dst, &p.map_a, kt * 128, c.tr * 128, full(stage), pol_a);
-            tma_load_2d(dst + Cfg::A_BYTES, &p.map_b, kt * 128, c.tc * BN, full(stage), pol_b);
+            tma_load_2d(dst + off_w, map_w, kt * 128, w_row(c), full(stage), pol_w);
+            tma_load_2d(dst + off_x, map_x, kt * 128, x_row(c), full(stage), pol_x);
             stage_seq[stage] = seq;
           }
         }
@@ -317,8 +353,59 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
     bool ok = true;
     int out_chunk = 0;  // normal mode: alternates between the two staging buffers
 
+    // Scale sources of a unit.  Normal: sa per row (thread), sb per
+    // 128-column block (warpgroup).  Swapped: sb per 128-row tile (CTA), sa
+    // per token column; lane j loads token col0 + j (and col0 + 32 + j when
+    // BN = 64).
+    struct ScaleSrc {
+      const float* sa;
+      const float* sa2;
+      const float* sb;
+      bool sa_ok, sa2_ok, sb_ok;
+    };
+    auto scale_src = [&](const UnitCoord& c) {
+      ScaleSrc q{p.sa, p.sa, p.sb, false, false, false};
+      const int col0 = c.tc * BN + g * COLS;
+      if constexpr (!SWAP) {
+        const int r = c.tr * 128 + row;
+        q.sa_ok = r < rows_total;
+        q.sa = p.sa + int64_t(q.sa_ok ? r : 0) * p.sa_m;
+        q.sb_ok = col0 < p.N;
+        q.sb = p.sb + int64_t(q.sb_ok ? col0 / 128 : 0) * p.sb_n;
+      } else {
+        const int t0 = col0 + lane, t1 = col0 + 32 + lane;
+        q.sa_ok = t0 < p.M && lane < BN;
+        q.sa = p.sa + int64_t(q.sa_ok ? t0 : 0) * p.sa_m;
+        if constexpr (BN > 32) {
+          q.sa2_ok = t1 < p.M;
+          q.sa2 = p.sa + int64_t(q.sa2_ok ? t1 : 0) * p.sa_m;
+        }
+        q.sb_ok = true;  // the tile's weight block exists (tr * 128 < N)
+        q.sb = p.sb + int64_t(c.tr) * p.sb_n;
+      }
+      return q;
+    };
+    // Scales of the next PF K blocks, in flight ahead of their use.
+    float pa[PF], pa2[PF], pb[PF];
+    auto load_scales = [&](const ScaleSrc& q, int kt, int j) {
+      pa[j] = q.sa_ok ? __ldg(q.sa + int64_t(kt) * p.sa_k) : 0.f;
+      if constexpr (SWAP && BN > 32) pa2[j] = q.sa2_ok ? __ldg(q.sa2 + int64_t(kt) * p.sa_k) : 0.f;
+      pb[j] = q.sb_ok ? __ldg(q.sb + int64_t(kt) * p.sb_k) : 0.f;
+    };
+    auto prefetch_unit = [&](const ScaleSrc& q, const UnitCoord& c) {
+#pragma unroll
+      for (int j = 0; j < PF; ++j)
+        if (c.kt0 + j < c.kt1) load_scales(q, c.kt0 + j, j);
+    };
+
+    griddep_wait();  // activation scales are the previous kernel's output
+    UnitCoord c_next = unit_coord(p, blockIdx.x < p.units ? blockIdx.x : 0);
+    ScaleSrc src_next = scale_src(c_next);
+    if (blockIdx.x < p.units) prefetch_unit(src_next, c_next);
+
     for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
-      const UnitCoord c = unit_coord(p, u);
+      const UnitCoord c = c_next;
+      const ScaleSrc src = src_next;
       const int r = c.tr * 128 + row;                       // this thread's MMA row
       const bool row_ok = r < rows_total;
       const bool warp_rows = c.tr * 128 + 32 * quarter < rows_total;  // warp-uniform
@@ -326,39 +413,6 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
       const int cols_total = SWAP ? p.M : p.N;
       const bool cols_ok = col0 < cols_total;               // warp-uniform
       const bool work = warp_rows && cols_ok;
-
-      // Scale sources.  Normal: sa per row (thread), sb per 128-column block
-      // (warpgroup).  Swapped: sb per 128-row tile (CTA), sa per token
-      // column; lane j loads token col0 + j (and col0 + 32 + j when BN = 64).
-      const float* sa_ptr;
-      const float* sa2_ptr = nullptr;
-      const float* sb_ptr;
-      bool sa_ok, sa2_ok = false, sb_ok;
-      if constexpr (!SWAP) {
-        sa_ok = row_ok;
-        sa_ptr = p.sa + int64_t(row_ok ? r : 0) * p.sa_m;
-        sb_ok = cols_ok;
-        sb_ptr = p.sb + int64_t(cols_ok ? col0 / 128 : 0) * p.sb_n;
-      } else {
-        const int t0 = col0 + lane, t1 = col0 + 32 + lane;
-        sa_ok = t0 < p.M && lane < BN;
-        sa_ptr = p.sa + int64_t(sa_ok ? t0 : 0) * p.sa_m;
-        if constexpr (BN > 32) {
-          sa2_ok = t1 < p.M;
-          sa2_ptr = p.sa + int64_t(sa2_ok ? t1 : 0) * p.sa_m;
-        }
-        sb_ok = true;  // the tile's weight block exists (tr * 128 < N)
-        sb_ptr = p.sb + int64_t(c.tr) * p.sb_n;
-      }
-      float pa[PF], pa2[PF], pb[PF];
-      auto load_scales = [&](int kt, int j) {
-        pa[j] = sa_ok ? __ldg(sa_ptr + int64_t(kt) * p.sa_k) : 0.f;
-        if constexpr (SWAP && BN > 32) pa2[j] = sa2_ok ? __ldg(sa2_ptr + int64_t(kt) * p.sa_k) : 0.f;
-        pb[j] = sb_ok ? __ldg(sb_ptr + int64_t(kt) * p.sb_k) : 0.f;
-      };
-#pragma unroll
-      for (int j = 0; j < PF; ++j)
-        if (c.kt0 + j < c.kt1) load_scales(c.kt0 + j, j);
 
       float accum[COLS];
 #pragma unroll
@@ -372,7 +426,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
             const float sa_v = pa[j], sb_v = pb[j];
             float sa2_v = 0.f;
             if constexpr (SWAP && BN > 32) sa2_v = pa2[j];
-            if (kt + PF < c.kt1) load_scales(kt + PF, j);
+            if (kt + PF < c.kt1) load_scales(src, kt + PF, j);
             ok = mbar_wait(acc_full(acc), acc_phase, abort_flag, kWaitAccFull) && ok;
             tc_fence_after();
             if (work) {
@@ -411,6 +465,14 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
             }
           }
         }
+      }
+
+      // The next unit's first scales go out now, ahead of this unit's
+      // split-K hand-off and store.
+      if (u + int(gridDim.x) < p.units) {
+        c_next = unit_coord(p, u + gridDim.x);
+        src_next = scale_src(c_next);
+        prefetch_unit(src_next, c_next);
       }
 
       bool store = work;

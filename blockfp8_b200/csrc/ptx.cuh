@@ -168,6 +168,14 @@ __device__ __forceinline__ uint64_t policy_evict_normal() {
   return p;
 }
 
+// Programmatic dependent launch: the primary lets its dependent grid start
+// early; the dependent waits for the primary's completion (and memory) at the
+// first use of its output.  Both are no-ops without a PDL launch.
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // gpu-scope acquire-release fence (split-K counter hand-off).
 __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 

@@ -37,6 +37,9 @@ constexpr int kQuantRows = kQuantThreads / 16;  // rows per CTA task
 constexpr int kQuantGroups = 4;                 // groups per half-warp task
 
 __global__ void __launch_bounds__(kQuantThreads) quantize_kernel(const QuantParams p) {
+  // A GEMM launched behind this kernel with programmatic dependent launch may
+  // start now: it only reads our output after griddepcontrol.wait.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int lane16 = threadIdx.x & 15;
   const int half = threadIdx.x >> 4;  // 0 .. 15: the row within the task
   const int row_blocks = (p.M + kQuantRows - 1) / kQuantRows;
