@@ -343,11 +343,12 @@ def main():
     if not bf.native_available():
         raise RuntimeError("native libraries missing: run python -m blockfp8_b200.build")
 
+    from blockfp8_b200 import sharding
     name, m = HEADLINE
     n, k = LAYERS[name]
-    assert n % (128 * world) == 0, "N must split into multiple-of-128 slices"
-    n_per = n // world
-    b, sb = make_weights(n, k, dev, seed=0, rows=(rank * n_per, (rank + 1) * n_per))
+    lo, hi = sharding.block_slices(n, world, rank)  # contiguous multiple-of-128 column slice
+    n_per = hi - lo
+    b, sb = make_weights(n, k, dev, seed=0, rows=(lo, hi))
     x_cpu = make_x(m, k, seed=0)
     x = x_cpu.to(dev)
     flush = Flusher(dev)
@@ -382,7 +383,7 @@ def main():
     q, s = bf.quantize_cuda(x)
     quant_us, _ = time_device(lambda: bf.quantize_cuda(x), args.steps, flush)
     gemm_med, gemm_us = time_device(lambda: bf.gemm(q, s, b, sb), args.steps, flush)
-    gemm_tflops = fp8_gemm_flops(m, n_per, k) / (gemm_us * 1e-6) / 1e12
+    gemm_tflops = fp8_gemm_flops(m, n_per, k) / (gemm_us * 1e-6) / 1e12  # this rank's slice
     pk = peaks()
     fp8_peak = 2.0 * pk["bf16_tflops"]
 
