@@ -48,6 +48,11 @@ struct ConfigEntry {
   bool swap;  // MMA rows are weight rows, columns are tokens (decode)
   const void* kernel;
   void (*launch)(const GemmParams&, int grid, cudaStream_t);
+  // Swapped configurations also come with the activation quantization done
+  // inside the kernel (bf16 in), used by fused plans.
+  const void* kernel_fused = nullptr;
+  void (*launch_fused)(const GemmParams&, int grid, cudaStream_t) = nullptr;
+  int smem_fused = 0, threads_fused = 0;
 };
 
 template <class Cfg>
@@ -71,6 +76,16 @@ ConfigEntry entry(const char* name) {
           reinterpret_cast<const void*>(&gemm_kernel<Cfg>), &launch_cfg<Cfg>};
 }
 
+template <class Cfg, class FusedCfg>
+ConfigEntry entry_fused(const char* name) {
+  ConfigEntry e = entry<Cfg>(name);
+  e.kernel_fused = reinterpret_cast<const void*>(&gemm_kernel<FusedCfg>);
+  e.launch_fused = &launch_cfg<FusedCfg>;
+  e.smem_fused = FusedCfg::SMEM_BYTES;
+  e.threads_fused = FusedCfg::THREADS;
+  return e;
+}
+
 // Normal order: "m128n<BN>": 128 activation rows x BN weight rows per tile.
 // Swapped order: "w128t<BN>": 128 weight rows x BN tokens per tile (decode).
 //                        BN  stages  swapped
@@ -80,10 +95,18 @@ using Cfg64 = GemmCfg<64, 8, false>;
 using CfgW16 = GemmCfg<16, 10, true>;
 using CfgW32 = GemmCfg<32, 10, true>;
 using CfgW64 = GemmCfg<64, 8, true>;
+// ... with the bf16 staging of in-kernel quantization (fewer stages fit)
+using CfgW16Q = GemmCfg<16, 8, true, true>;
+using CfgW32Q = GemmCfg<32, 7, true, true>;
+using CfgW64Q = GemmCfg<64, 5, true, true>;
 
 const ConfigEntry kConfigs[] = {
-    entry<Cfg256>("m128n256s4"), entry<Cfg128>("m128n128s6"), entry<Cfg64>("m128n64s8"),
-    entry<CfgW16>("w128t16s10"), entry<CfgW32>("w128t32s10"), entry<CfgW64>("w128t64s8"),
+    entry<Cfg256>("m128n256s4"),
+    entry<Cfg128>("m128n128s6"),
+    entry<Cfg64>("m128n64s8"),
+    entry_fused<CfgW16, CfgW16Q>("w128t16s10"),
+    entry_fused<CfgW32, CfgW32Q>("w128t32s10"),
+    entry_fused<CfgW64, CfgW64Q>("w128t64s8"),
 };
 constexpr int kNumConfigs = int(sizeof(kConfigs) / sizeof(kConfigs[0]));
 // The fused path (gemm_bf16) quantizes into the workspace, then runs the
@@ -116,15 +139,24 @@ int current_device_sms(int* dev_out) {
 
 // The dynamic shared-memory limit is a per-device attribute of a kernel:
 // set it on the first launch of each configuration on each device.
-int ensure_smem_attr(int config, int dev) {
-  static std::atomic<uint64_t> done[kNumConfigs] = {};
+int ensure_smem_attr(int config, int dev, bool in_kernel_quant) {
+  static std::atomic<uint64_t> done[2][kNumConfigs] = {};
   const uint64_t bit = dev < 64 ? (uint64_t(1) << dev) : 0;
-  if (bit && (done[config].load(std::memory_order_acquire) & bit)) return BFP8_OK;
+  std::atomic<uint64_t>& d = done[in_kernel_quant ? 1 : 0][config];
+  if (bit && (d.load(std::memory_order_acquire) & bit)) return BFP8_OK;
   const ConfigEntry& e = kConfigs[config];
-  cudaError_t err = cudaFuncSetAttribute(e.kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, e.smem);
+  cudaError_t err = cudaFuncSetAttribute(in_kernel_quant ? e.kernel_fused : e.kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         in_kernel_quant ? e.smem_fused : e.smem);
   if (err != cudaSuccess) return cuda_fail(err, "cudaFuncSetAttribute(MaxDynamicSharedMemorySize)");
-  done[config].fetch_or(bit, std::memory_order_release);
+  d.fetch_or(bit, std::memory_order_release);
   return BFP8_OK;
+}
+
+// Fused plans of swapped configurations quantize inside the GEMM kernel;
+// the others run the quantization kernel into the workspace first.
+bool quantizes_in_kernel(const bfp8_plan& plan) {
+  return plan.fused && kConfigs[plan.config].launch_fused != nullptr;
 }
 
 // ---- tensor maps --------------------------------------------------------------------
@@ -394,7 +426,8 @@ int bfp8_plan_shape(const bfp8_gemm_problem* p, bfp8_plan plan, int* tiles, int*
 int64_t bfp8_workspace_bytes(const bfp8_gemm_problem* p, bfp8_plan plan) {
   if (!p || !config_ok(plan.config)) return fail(BFP8_EINVAL, "bad config id");
   if (p->M <= 0) return 0;
-  return (plan.fused ? fused_front_bytes(*p) : 0) + splitk_bytes(*p, plan);
+  const bool front = plan.fused && !quantizes_in_kernel(plan);
+  return (front ? fused_front_bytes(*p) : 0) + splitk_bytes(*p, plan);
 }
 
 int bfp8_counters_needed(const bfp8_gemm_problem* p, bfp8_plan plan) {
@@ -437,11 +470,13 @@ int bfp8_launch_gemm(const bfp8_gemm_problem* pp, bfp8_plan plan, float* workspa
   if (sms <= 0) return cuda_fail(cudaGetLastError(), "cudaGetDevice");
 
   const Derived d = derive(p, plan);
-  if ((fused || d.splits > 1) && !workspace) return fail(BFP8_EINVAL, "workspace required");
+  const bool in_kernel = quantizes_in_kernel(plan);
+  if (((fused && !in_kernel) || d.splits > 1) && !workspace) return fail(BFP8_EINVAL, "workspace required");
   if (d.splits > 1 && !counters) return fail(BFP8_EINVAL, "split-K counters required");
 
   uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
-  if (fused) {
+  const void* x_bf16 = p.a;
+  if (fused && !in_kernel) {
     // gemm_bf16: quantize x into the front of the workspace (M-major
     // scales), then the GEMM reads it like any quantized input.
     uint8_t* q = ws;
@@ -460,13 +495,21 @@ int bfp8_launch_gemm(const bfp8_gemm_problem* pp, bfp8_plan plan, float* workspa
   const ConfigEntry& e = kConfigs[plan.config];
   GemmParams gp;
   std::memset(&gp, 0, sizeof(gp));
+  if (in_kernel) {
+    // The kernel reads bf16 activation tiles [BN tokens x 128] and quantizes
+    // them itself; operand B's map is not used.
+    if (int r = make_map(&gp.map_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x_bf16, uint64_t(p.K), uint64_t(p.M),
+                         uint64_t(p.lda) * 2, 128, uint32_t(e.bn), CU_TENSOR_MAP_SWIZZLE_NONE))
+      return r;
+    gp.eps = p.eps;
+  }
   // Operand tiles: 128 rows of the MMA A operand, BN rows of the B operand,
   // one 128-byte K block each, 128-byte swizzle.  Activations are A in the
   // normal order and B in the swapped one.
   const void* a_src = e.swap ? p.b : p.a;
-  const void* b_src = e.swap ? p.a : p.b;
-  const int64_t a_ld = e.swap ? p.ldb : p.lda, b_ld = e.swap ? p.lda : p.ldb;
-  const int a_rows = e.swap ? p.N : p.M, b_rows = e.swap ? p.M : p.N;
+  const void* b_src = in_kernel ? p.b : (e.swap ? p.a : p.b);  // in-kernel: placeholder, unused
+  const int64_t a_ld = e.swap ? p.ldb : p.lda, b_ld = (e.swap && !in_kernel) ? p.lda : p.ldb;
+  const int a_rows = e.swap ? p.N : p.M, b_rows = in_kernel ? p.N : (e.swap ? p.M : p.N);
   if (int r = make_map(&gp.map_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, a_src, uint64_t(p.K),
                        uint64_t(a_rows), uint64_t(a_ld), 128, 128, CU_TENSOR_MAP_SWIZZLE_128B))
     return r;
@@ -507,11 +550,11 @@ int bfp8_launch_gemm(const bfp8_gemm_problem* pp, bfp8_plan plan, float* workspa
   const int64_t a_bytes = int64_t(d.tiles_r) * 128 * p.K;
   gp.group_r = e.swap || a_bytes <= (int64_t(48) << 20) ? d.tiles_r : 8;
   gp.stream_b = (e.swap || p.M <= 128) ? 1 : 0;  // weights read once: evict them first
-  gp.pdl = fused ? 1 : 0;
+  gp.pdl = fused && !in_kernel ? 1 : 0;
 
-  if (int r = ensure_smem_attr(plan.config, dev)) return r;
+  if (int r = ensure_smem_attr(plan.config, dev, in_kernel)) return r;
   const int grid = std::min(gp.units, sms);
-  e.launch(gp, grid, stream);
+  (in_kernel ? e.launch_fused : e.launch)(gp, grid, stream);
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return cuda_fail(err, "GEMM kernel launch");
   return BFP8_OK;

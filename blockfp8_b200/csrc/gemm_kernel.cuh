@@ -47,6 +47,7 @@
 
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp8.h>
 
 #include <cstdint>
 
@@ -71,12 +72,19 @@ struct GemmParams {
   int group_r;  // raster: groups of group_r row tiles, rows fastest inside a group
   int stream_b;  // 1: weights are read once (decode): L2 evict-first for them
   int pdl;       // 1: launched right behind our quantizer with programmatic dependent launch
+  CUtensorMap map_x;  // in-kernel quantization: bf16 activations [M, K], box 128 x BN
+  float eps;          // in-kernel quantization: floor of each group's amax
 };
 
-template <int BN_, int STAGES_, bool SWAP_>
+template <int BN_, int STAGES_, bool SWAP_, bool FUSE_ = false>
 struct GemmCfg {
   static constexpr int BM = 128, BN = BN_, BK = 128, STAGES = STAGES_;
   static constexpr bool SWAP = SWAP_;
+  // FUSE: the activations arrive as bf16 and a quantizer warp turns each K
+  // block of them into the e4m3 B operand and per-token scales in the kernel
+  // (swapped order only: the tokens are the B operand).
+  static constexpr bool FUSE = FUSE_;
+  static_assert(!FUSE || SWAP, "in-kernel quantization needs the swapped order");
   static_assert(SWAP ? (BN == 16 || BN == 32 || BN == 64) : (BN == 64 || BN == 128 || BN == 256),
                 "unsupported tile");
   static constexpr int COLS = SWAP ? BN : (BN < 128 ? BN : 128);  // accumulators per thread
@@ -104,15 +112,19 @@ struct GemmCfg {
   static constexpr int TMEM_COLS = ACC_BUFS * BN < 32 ? 32 : ACC_BUFS * BN;
   static constexpr int A_BYTES = BM * BK;
   static constexpr int B_BYTES = BN * BK;
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int X_BYTES = FUSE ? BN * BK * 2 : 0;  // bf16 staging of one K block
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + X_BYTES;
+  static constexpr int FULL_TX = FUSE ? A_BYTES : A_BYTES + B_BYTES;  // TMA bytes per "full"
   // Output staging per epilogue warp: normal, two [32 rows x 32 bf16] chunk
   // buffers (64-byte swizzle); swapped, one [BN tokens x 32 bf16] tile.
   static constexpr int OUT_BYTES = SWAP ? BN * 64 : 2 * 32 * 64;
   static constexpr int SMEM_TILES = STAGES * STAGE_BYTES;
   static constexpr int SMEM_OUT = ((EPI_WARPS * OUT_BYTES + 1023) / 1024) * 1024;
-  static constexpr int NUM_BARS = 2 * STAGES + 2 * ACC_BUFS + 1;
+  static constexpr int SMEM_SCALES = FUSE ? ACC_BUFS * BN * 4 : 0;  // per-token scales, per buffer
+  static constexpr int NUM_BARS = 2 * STAGES + 2 * ACC_BUFS + 1 + (FUSE ? STAGES + ACC_BUFS : 0);
   static constexpr int SMEM_MISC = 16 + 4 * STAGES;  // TMEM slot, flags, last load per stage
-  static constexpr int SMEM_BYTES = 1024 + SMEM_TILES + SMEM_OUT + NUM_BARS * 8 + SMEM_MISC;
+  static constexpr int SMEM_BYTES =
+      1024 + SMEM_TILES + SMEM_OUT + SMEM_SCALES + NUM_BARS * 8 + SMEM_MISC;
   static_assert(SMEM_BYTES <= 232448, "more shared memory than one sm_100 CTA can have");
   static_assert(TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM allocation");
   static_assert(STAGE_BYTES % 1024 == 0, "stages must stay 1024-byte aligned");
@@ -177,13 +189,17 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
   uint8_t* smem = smem_raw + (base - raw);
   const uint32_t s_tiles = base;
   const uint32_t s_out = base + Cfg::SMEM_TILES;
-  const uint32_t s_bars = s_out + Cfg::SMEM_OUT;
+  const uint32_t s_scales = s_out + Cfg::SMEM_OUT;  // FUSE: [ACC_BUFS][BN] fp32
+  const uint32_t s_bars = s_scales + Cfg::SMEM_SCALES;
   auto full = [&](int s) { return s_bars + 8u * s; };
   auto empty = [&](int s) { return s_bars + 8u * (STAGES + s); };
   auto acc_full = [&](int a) { return s_bars + 8u * (2 * STAGES + a); };
   auto acc_empty = [&](int a) { return s_bars + 8u * (2 * STAGES + ACC_BUFS + a); };
   const uint32_t mma_done = s_bars + 8u * (2 * STAGES + 2 * ACC_BUFS);
-  uint32_t* misc = reinterpret_cast<uint32_t*>(smem + Cfg::SMEM_TILES + Cfg::SMEM_OUT + 8 * Cfg::NUM_BARS);
+  auto xfull = [&](int s) { return s_bars + 8u * (2 * STAGES + 2 * ACC_BUFS + 1 + s); };
+  auto scale_ready = [&](int a) { return s_bars + 8u * (3 * STAGES + 2 * ACC_BUFS + 1 + a); };
+  uint32_t* misc = reinterpret_cast<uint32_t*>(smem + Cfg::SMEM_TILES + Cfg::SMEM_OUT + Cfg::SMEM_SCALES +
+                                               8 * Cfg::NUM_BARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 1);
   volatile int* last_flag = reinterpret_cast<volatile int*>(misc + 2);
   volatile int* stage_seq = reinterpret_cast<volatile int*>(misc + 4);  // last K block loaded per stage
@@ -192,9 +208,12 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(full(s), 1);
+      mbar_init(full(s), Cfg::FUSE ? 2 : 1);  // FUSE: the weight TMA + the quantizer warp
       mbar_init(empty(s), 1);
+      if constexpr (Cfg::FUSE) mbar_init(xfull(s), 1);
     }
+    if constexpr (Cfg::FUSE)
+      for (int a = 0; a < ACC_BUFS; ++a) mbar_init(scale_ready(a), 1);
     for (int a = 0; a < ACC_BUFS; ++a) {
       mbar_init(acc_full(a), 1);
       mbar_init(acc_empty(a), Cfg::EPI_WARPS);
@@ -208,6 +227,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
     tma_prefetch_desc(&p.map_a);
     tma_prefetch_desc(&p.map_b);
     tma_prefetch_desc(&p.map_c);
+    if constexpr (Cfg::FUSE) tma_prefetch_desc(&p.map_x);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(misc), Cfg::TMEM_COLS);
@@ -226,9 +246,93 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
     // two threads in parallel.  K block i of the sequence always uses smem
     // stage i % STAGES (phase (i / STAGES) & 1) and TMEM buffer i % ACC_BUFS
     // (phase (i / ACC_BUFS) & 1), whoever handles it.
-    const bool producer = warp == 0 || warp == 3;
+    // FUSE: warp 0 is the only producer (weights + bf16 activation tiles
+    // for every K block) and warp 3 the quantizer warp.
+    const bool producer = Cfg::FUSE ? warp == 0 : (warp == 0 || warp == 3);
+    const bool quantizer = Cfg::FUSE && warp == 3;
     const int role = (warp == 0 || warp == 1) ? 0 : 1;  // which half of the K blocks
-    if (lane == 0) {
+    auto mine = [&](int seq) { return ((Cfg::FUSE && producer) || (seq & 1) == role); };
+    if (quantizer) {
+      if constexpr (Cfg::FUSE) {
+        // ------------------------------------------------------------ quantizer warp
+        // Per K block: the bf16 tile [BN tokens x 128] staged by TMA becomes
+        // the e4m3 B operand in the 128-byte swizzle the MMA expects, and
+        // each token's scale goes to the scale slot of the block's TMEM
+        // buffer.  Same arithmetic as quantize_kernel: amax from eps, IEEE
+        // amax / 448, clamp, round-to-nearest-even e4m3 with saturation.
+        // Rows past M and columns past K were zero-filled by the TMA, so they
+        // quantize to zero codes.
+        constexpr int LPR = BN >= 32 ? 1 : 32 / BN;  // lanes per token row
+        constexpr int RPL = BN >= 32 ? BN / 32 : 1;  // token rows per lane
+        constexpr int CPL = 16 / LPR;                // 16-byte bf16 chunks per lane per row
+        int seq = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
+          const UnitCoord c = unit_coord(p, u);
+          for (int kt = c.kt0; kt < c.kt1; ++kt, ++seq) {
+            const int stage = seq % STAGES, slot = seq % ACC_BUFS;
+            if (!mbar_wait(xfull(stage), uint32_t(seq / STAGES) & 1u, abort_flag, kWaitFull) ||
+                !mbar_wait(acc_empty(slot), (uint32_t(seq / ACC_BUFS) & 1u) ^ 1u, abort_flag,
+                           kWaitAccEmpty)) {
+              ok = false;
+              break;
+            }
+            const uint32_t st_base = s_tiles + uint32_t(stage) * Cfg::STAGE_BYTES;
+            const uint32_t b_tile = st_base + Cfg::A_BYTES;
+            const uint32_t x_tile = b_tile + Cfg::B_BYTES;
+#pragma unroll
+            for (int rr = 0; rr < RPL; ++rr) {
+              const int row = lane / LPR + rr * (32 / LPR);
+              const int part = lane % LPR;
+              uint4 v[CPL];
+#pragma unroll
+              for (int j = 0; j < CPL; ++j) {  // rotated start: 4 wavefronts per load
+                const int ch = part * CPL + ((j + lane) % CPL);
+                v[j] = ld_shared_v4(x_tile + uint32_t(row) * 256u + uint32_t(ch) * 16u);
+              }
+              float amax = p.eps;
+#pragma unroll
+              for (int j = 0; j < CPL; ++j) {
+                const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v[j]);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float2 f = __bfloat1622float2(h[e]);
+                  amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+                }
+              }
+#pragma unroll
+              for (int o = LPR / 2; o > 0; o >>= 1)
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+              const float scale = amax / 448.f;
+#pragma unroll
+              for (int j = 0; j < CPL; ++j) {
+                const int ch = part * CPL + ((j + lane) % CPL);  // 8 values -> 8 e4m3 bytes
+                const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v[j]);
+                uint32_t packed[2] = {0u, 0u};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float2 f = __bfloat1622float2(h[e]);
+                  const float2 q = make_float2(fminf(fmaxf(f.x / scale, -448.f), 448.f),
+                                               fminf(fmaxf(f.y / scale, -448.f), 448.f));
+                  const uint32_t pair = __nv_cvt_float2_to_fp8x2(q, __NV_SATFINITE, __NV_E4M3);
+                  packed[e >> 1] |= pair << (16 * (e & 1));
+                }
+                const uint32_t unit16 = uint32_t(ch >> 1) ^ uint32_t(row & 7);  // 128-byte swizzle
+                st_shared_v2(b_tile + uint32_t(row) * 128u + unit16 * 16u + uint32_t(ch & 1) * 8u,
+                             packed[0], packed[1]);
+              }
+              if (part == 0) st_shared_f32(s_scales + uint32_t(slot * BN + row) * 4u, scale);
+            }
+            fence_proxy_async_smem();  // the MMA reads the B tile through the async proxy
+            __syncwarp();
+            if (lane == 0) {
+              mbar_arrive(full(stage));
+              mbar_arrive(scale_ready(slot));
+            }
+          }
+        }
+      }
+    } else if (lane == 0) {
       if (producer) {
         // ------------------------------------------------------------ TMA producer
         // Activations are re-read by many tiles: keep them; weights streamed
@@ -256,9 +360,9 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
           for (int u = blockIdx.x; u < p.units && seq < STAGES; u += gridDim.x) {
             const UnitCoord c = unit_coord(p, u);
             for (int kt = c.kt0; kt < c.kt1 && seq < STAGES; ++kt, ++seq) {
-              if ((seq & 1) != role) continue;
+              if (!mine(seq)) continue;
               const uint32_t dst = s_tiles + uint32_t(seq) * Cfg::STAGE_BYTES;  // stage = seq
-              mbar_arrive_expect_tx(full(seq), Cfg::STAGE_BYTES);
+              mbar_arrive_expect_tx(full(seq), Cfg::FULL_TX);
               tma_load_2d(dst + off_w, map_w, kt * 128, w_row(c), full(seq), pol_w);
               stage_seq[seq] = seq;
             }
@@ -271,7 +375,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
         for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
           const UnitCoord c = unit_coord(p, u);
           for (int kt = c.kt0; kt < c.kt1; ++kt, ++seq) {
-            if ((seq & 1) != role) continue;
+            if (!mine(seq)) continue;
             const int stage = seq % STAGES;
             const uint32_t dst = s_tiles + uint32_t(stage) * Cfg::STAGE_BYTES;
             if (seq < early) {  // weights already requested; add the activations
@@ -283,9 +387,15 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
               ok = false;
               break;
             }
-            mbar_arrive_expect_tx(full(stage), Cfg::STAGE_BYTES);
+            mbar_arrive_expect_tx(full(stage), Cfg::FULL_TX);
             tma_load_2d(dst + off_w, map_w, kt * 128, w_row(c), full(stage), pol_w);
-            tma_load_2d(dst + off_x, map_x, kt * 128, x_row(c), full(stage), pol_x);
+            if constexpr (Cfg::FUSE) {  // bf16 activations into the stage's staging area
+              mbar_arrive_expect_tx(xfull(stage), Cfg::X_BYTES);
+              tma_load_2d(dst + Cfg::A_BYTES + Cfg::B_BYTES, &p.map_x, kt * 128, c.tc * BN, xfull(stage),
+                          pol_x);
+            } else {
+              tma_load_2d(dst + off_x, map_x, kt * 128, x_row(c), full(stage), pol_x);
+            }
             stage_seq[stage] = seq;
           }
         }
@@ -327,15 +437,18 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
       }
     }
     __syncwarp();  // reconverge before the barriers below (bar.sync is .aligned)
-    if (producer) {
+    if (warp == 0 || warp == 3) {
       // Every issued copy must land before the CTA exits.  On the normal path
       // the MMA threads have seen them all; after an abort, wait on the last
       // load of each stage (its phase completes when its bytes arrive).
-      named_bar_sync(2, 64);  // both producers are done issuing
+      named_bar_sync(2, 64);  // warps 0 and 3 are done issuing (and quantizing)
       if (warp == 0 && lane == 0)
         for (int st = 0; st < STAGES; ++st)
-          if (stage_seq[st] >= 0)
-            mbar_wait(full(st), uint32_t(stage_seq[st] / STAGES) & 1u, nullptr, kWaitDrain);
+          if (stage_seq[st] >= 0) {
+            const uint32_t ph = uint32_t(stage_seq[st] / STAGES) & 1u;
+            if constexpr (Cfg::FUSE) mbar_wait(xfull(st), ph, nullptr, kWaitDrain);
+            mbar_wait(full(st), ph, nullptr, kWaitDrain);
+          }
       __syncwarp();
     }
   } else {
@@ -374,10 +487,10 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
         q.sb = p.sb + int64_t(q.sb_ok ? col0 / 128 : 0) * p.sb_n;
       } else {
         const int t0 = col0 + lane, t1 = col0 + 32 + lane;
-        q.sa_ok = t0 < p.M && lane < BN;
+        q.sa_ok = !Cfg::FUSE && t0 < p.M && lane < BN;  // FUSE: scales come from smem
         q.sa = p.sa + int64_t(q.sa_ok ? t0 : 0) * p.sa_m;
         if constexpr (BN > 32) {
-          q.sa2_ok = t1 < p.M;
+          q.sa2_ok = !Cfg::FUSE && t1 < p.M;
           q.sa2 = p.sa + int64_t(q.sa2_ok ? t1 : 0) * p.sa_m;
         }
         q.sb_ok = true;  // the tile's weight block exists (tr * 128 < N)
@@ -429,6 +542,12 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
             if (kt + PF < c.kt1) load_scales(src, kt + PF, j);
             ok = mbar_wait(acc_full(acc), acc_phase, abort_flag, kWaitAccFull) && ok;
             tc_fence_after();
+            float sa_f = sa_v, sa2_f = sa2_v;
+            if constexpr (Cfg::FUSE) {  // this K block's token scales, from the quantizer warp
+              ok = mbar_wait(scale_ready(acc), acc_phase, abort_flag, kWaitAccFull) && ok;
+              sa_f = lane < BN ? ld_shared_f32(s_scales + uint32_t(acc * BN + lane) * 4u) : 0.f;
+              if constexpr (BN > 32) sa2_f = ld_shared_f32(s_scales + uint32_t(acc * BN + 32 + lane) * 4u);
+            }
             if (work) {
               const uint32_t t = t_lane + uint32_t(acc * BN + g * COLS);
               if constexpr (!SWAP) {
@@ -447,7 +566,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
                 for (int ch = 0; ch < BN / CH; ++ch) {
                   float part[CH];
                   tmem_ld<CH>(t + CH * ch, part);
-                  const float src = ch == 0 ? sa_v : sa2_v;
+                  const float src = ch == 0 ? sa_f : sa2_f;
 #pragma unroll
                   for (int i = 0; i < CH; ++i) {
                     const float scale = __shfl_sync(0xffffffffu, src, i) * sb_v;

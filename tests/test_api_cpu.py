@@ -154,7 +154,11 @@ def test_c_abi_answers_without_a_gpu():
         cnt = lib.bfp8_counters_needed(ctypes.byref(p), plan)
         splits = -(-kt.value // -(-kt.value // min(plan.splits, kt.value)))
         assert (ws == 0) == (splits == 1) and (cnt == 0) == (splits == 1)
-        assert lib.bfp8_workspace_bytes(ctypes.byref(p), fplan) >= m * k  # quantized x lives there
+        fws = lib.bfp8_workspace_bytes(ctypes.byref(p), fplan)
+        if names[fplan.config].startswith("m"):  # quantization kernel first: q and s live there
+            assert fws >= m * k
+        else:  # swapped tiles quantize inside the GEMM: only split-K scratch
+            assert fws == lib.bfp8_workspace_bytes(ctypes.byref(p), plan)
     bad = _native.Plan(99, 1, 0)
     p = _native.GemmProblem(M=1, N=128, K=128)
     assert lib.bfp8_workspace_bytes(ctypes.byref(p), bad) < 0
