@@ -53,6 +53,7 @@ struct ConfigEntry {
   const void* kernel_fused = nullptr;
   void (*launch_fused)(const GemmParams&, int grid, cudaStream_t) = nullptr;
   int smem_fused = 0, threads_fused = 0;
+  int act_kb = 0;  // K blocks of one unit the in-kernel variant keeps resident
 };
 
 template <class Cfg>
@@ -83,6 +84,7 @@ ConfigEntry entry_fused(const char* name) {
   e.launch_fused = &launch_cfg<FusedCfg>;
   e.smem_fused = FusedCfg::SMEM_BYTES;
   e.threads_fused = FusedCfg::THREADS;
+  e.act_kb = FusedCfg::ACT_KB;
   return e;
 }
 
@@ -95,10 +97,11 @@ using Cfg64 = GemmCfg<64, 8, false>;
 using CfgW16 = GemmCfg<16, 10, true>;
 using CfgW32 = GemmCfg<32, 10, true>;
 using CfgW64 = GemmCfg<64, 8, true>;
-// ... with the bf16 staging of in-kernel quantization (fewer stages fit)
-using CfgW16Q = GemmCfg<16, 8, true, true>;
-using CfgW32Q = GemmCfg<32, 7, true, true>;
-using CfgW64Q = GemmCfg<64, 5, true, true>;
+// ... quantizing in the kernel: the unit's B operand is resident (64 KB),
+// the ring carries only weight tiles
+using CfgW16Q = GemmCfg<16, 9, true, true>;
+using CfgW32Q = GemmCfg<32, 9, true, true>;
+using CfgW64Q = GemmCfg<64, 8, true, true>;
 
 const ConfigEntry kConfigs[] = {
     entry<Cfg256>("m128n256s4"),
@@ -153,10 +156,17 @@ int ensure_smem_attr(int config, int dev, bool in_kernel_quant) {
   return BFP8_OK;
 }
 
-// Fused plans of swapped configurations quantize inside the GEMM kernel;
-// the others run the quantization kernel into the workspace first.
-bool quantizes_in_kernel(const bfp8_plan& plan) {
-  return plan.fused && kConfigs[plan.config].launch_fused != nullptr;
+struct Derived {
+  int tiles_r, tiles_c, tiles, k_tiles, k_per_split, splits;
+};
+Derived derive(const bfp8_gemm_problem& p, const bfp8_plan& plan);
+
+// Fused plans of swapped configurations whose units fit the resident operand
+// quantize inside the GEMM kernel; the others run the quantization kernel
+// into the workspace first (same results either way).
+bool quantizes_in_kernel(const bfp8_gemm_problem& p, const bfp8_plan& plan) {
+  const ConfigEntry& e = kConfigs[plan.config];
+  return plan.fused && e.launch_fused != nullptr && derive(p, plan).k_per_split <= e.act_kb;
 }
 
 // ---- tensor maps --------------------------------------------------------------------
@@ -288,10 +298,6 @@ const TableEntry* balanced_entry(const TableEntry* above, int M, int N, int K, i
   }
   return best;
 }
-
-struct Derived {
-  int tiles_r, tiles_c, tiles, k_tiles, k_per_split, splits;
-};
 
 Derived derive(const bfp8_gemm_problem& p, const bfp8_plan& plan) {
   const ConfigEntry& e = kConfigs[plan.config];
@@ -426,7 +432,7 @@ int bfp8_plan_shape(const bfp8_gemm_problem* p, bfp8_plan plan, int* tiles, int*
 int64_t bfp8_workspace_bytes(const bfp8_gemm_problem* p, bfp8_plan plan) {
   if (!p || !config_ok(plan.config)) return fail(BFP8_EINVAL, "bad config id");
   if (p->M <= 0) return 0;
-  const bool front = plan.fused && !quantizes_in_kernel(plan);
+  const bool front = plan.fused && !quantizes_in_kernel(*p, plan);
   return (front ? fused_front_bytes(*p) : 0) + splitk_bytes(*p, plan);
 }
 
@@ -470,7 +476,7 @@ int bfp8_launch_gemm(const bfp8_gemm_problem* pp, bfp8_plan plan, float* workspa
   if (sms <= 0) return cuda_fail(cudaGetLastError(), "cudaGetDevice");
 
   const Derived d = derive(p, plan);
-  const bool in_kernel = quantizes_in_kernel(plan);
+  const bool in_kernel = quantizes_in_kernel(p, plan);
   if (((fused && !in_kernel) || d.splits > 1) && !workspace) return fail(BFP8_EINVAL, "workspace required");
   if (d.splits > 1 && !counters) return fail(BFP8_EINVAL, "split-K counters required");
 
@@ -496,11 +502,10 @@ int bfp8_launch_gemm(const bfp8_gemm_problem* pp, bfp8_plan plan, float* workspa
   GemmParams gp;
   std::memset(&gp, 0, sizeof(gp));
   if (in_kernel) {
-    // The kernel reads bf16 activation tiles [BN tokens x 128] and quantizes
-    // them itself; operand B's map is not used.
-    if (int r = make_map(&gp.map_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x_bf16, uint64_t(p.K), uint64_t(p.M),
-                         uint64_t(p.lda) * 2, 128, uint32_t(e.bn), CU_TENSOR_MAP_SWIZZLE_NONE))
-      return r;
+    // The kernel reads the bf16 activations and quantizes them itself;
+    // operand B's tensor map is not used.
+    gp.x = static_cast<const __nv_bfloat16*>(x_bf16);
+    gp.ldx = p.lda;
     gp.eps = p.eps;
   }
   // Operand tiles: 128 rows of the MMA A operand, BN rows of the B operand,

@@ -6,10 +6,9 @@
 // units (an output tile and a range of 128-wide K blocks):
 //
 //   warps 0, 3  TMA producers (one thread each, alternate K blocks): the
-//               two operand tiles of each K block (128-byte swizzle, 128
-//               bytes = one K block per row) into a STAGES-deep
-//               shared-memory ring; completion is counted in bytes on the
-//               stage's "full" mbarrier;
+//               operand tiles of each K block (128-byte swizzle, 128 bytes =
+//               one K block per row) into a STAGES-deep shared-memory ring;
+//               completion is counted in bytes on the stage's "full" mbarrier;
 //   warps 1, 2  MMA issuers (one thread each, alternate K blocks): four
 //               tcgen05.mma.kind::f8f6f4 (K = 32 each, e4m3 x e4m3 -> f32)
 //               into one of ACC_BUFS tensor-memory (TMEM) partial buffers,
@@ -32,6 +31,14 @@
 // a K block is spread over all 128 TMEM lanes (4 warps) instead of the one
 // warp that may read lanes 0-31.  Every output element is the same sum of
 // the same products in both orders.
+//
+// In-kernel quantization (FUSE, swapped order): the activations arrive as
+// bf16.  At the start of each unit the epilogue warps quantize the unit's
+// tokens x K range into a resident shared-memory copy of the B operand (the
+// same 128-byte swizzle the TMA would write) plus per-token scales, with the
+// arithmetic of the quantization kernel, and release it to the MMA issuers;
+// the weight tiles stream into the stage ring meanwhile.  One kernel, no
+// dependency on a previous one.
 //
 // Because every K block gets its own TMEM buffer, the MMAs of block k + 1
 // run while block k is promoted.  With split-K the units of one tile cover
@@ -72,21 +79,19 @@ struct GemmParams {
   int group_r;  // raster: groups of group_r row tiles, rows fastest inside a group
   int stream_b;  // 1: weights are read once (decode): L2 evict-first for them
   int pdl;       // 1: launched right behind our quantizer with programmatic dependent launch
-  CUtensorMap map_x;  // in-kernel quantization: bf16 activations [M, K], box 128 x BN
-  float eps;          // in-kernel quantization: floor of each group's amax
+  const __nv_bfloat16* x;  // in-kernel quantization: bf16 activations [M, K], row stride ldx
+  int64_t ldx;
+  float eps;  // in-kernel quantization: floor of each group's amax
 };
 
 template <int BN_, int STAGES_, bool SWAP_, bool FUSE_ = false>
 struct GemmCfg {
   static constexpr int BM = 128, BN = BN_, BK = 128, STAGES = STAGES_;
   static constexpr bool SWAP = SWAP_;
-  // FUSE: the activations arrive as bf16 and a quantizer warp turns each K
-  // block of them into the e4m3 B operand and per-token scales in the kernel
-  // (swapped order only: the tokens are the B operand).
   static constexpr bool FUSE = FUSE_;
-  static_assert(!FUSE || SWAP, "in-kernel quantization needs the swapped order");
   static_assert(SWAP ? (BN == 16 || BN == 32 || BN == 64) : (BN == 64 || BN == 128 || BN == 256),
                 "unsupported tile");
+  static_assert(!FUSE || SWAP, "in-kernel quantization needs the swapped order");
   static constexpr int COLS = SWAP ? BN : (BN < 128 ? BN : 128);  // accumulators per thread
   static constexpr int EPI_WG = SWAP ? 1 : BN / COLS;
   static constexpr int EPI_WARPS = 4 * EPI_WG;
@@ -112,22 +117,24 @@ struct GemmCfg {
   static constexpr int TMEM_COLS = ACC_BUFS * BN < 32 ? 32 : ACC_BUFS * BN;
   static constexpr int A_BYTES = BM * BK;
   static constexpr int B_BYTES = BN * BK;
-  static constexpr int X_BYTES = FUSE ? BN * BK * 2 : 0;  // bf16 staging of one K block
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + X_BYTES;
-  static constexpr int FULL_TX = FUSE ? A_BYTES : A_BYTES + B_BYTES;  // TMA bytes per "full"
+  // FUSE: the B operand of a whole unit stays resident (ACT_KB K blocks at
+  // most, 64 KB), so the ring only carries weight tiles.
+  static constexpr int ACT_KB = FUSE ? 65536 / B_BYTES : 0;
+  static constexpr int SMEM_ACT = ACT_KB * B_BYTES;
+  static constexpr int SMEM_ACT_SCALES = ACT_KB * BN * 4;
+  static constexpr int STAGE_BYTES = FUSE ? A_BYTES : A_BYTES + B_BYTES;
   // Output staging per epilogue warp: normal, two [32 rows x 32 bf16] chunk
   // buffers (64-byte swizzle); swapped, one [BN tokens x 32 bf16] tile.
   static constexpr int OUT_BYTES = SWAP ? BN * 64 : 2 * 32 * 64;
   static constexpr int SMEM_TILES = STAGES * STAGE_BYTES;
   static constexpr int SMEM_OUT = ((EPI_WARPS * OUT_BYTES + 1023) / 1024) * 1024;
-  static constexpr int SMEM_SCALES = FUSE ? ACC_BUFS * BN * 4 : 0;  // per-token scales, per buffer
-  static constexpr int NUM_BARS = 2 * STAGES + 2 * ACC_BUFS + 1 + (FUSE ? STAGES + ACC_BUFS : 0);
+  static constexpr int NUM_BARS = 2 * STAGES + 2 * ACC_BUFS + 2;
   static constexpr int SMEM_MISC = 16 + 4 * STAGES;  // TMEM slot, flags, last load per stage
   static constexpr int SMEM_BYTES =
-      1024 + SMEM_TILES + SMEM_OUT + SMEM_SCALES + NUM_BARS * 8 + SMEM_MISC;
+      1024 + SMEM_TILES + SMEM_ACT + SMEM_OUT + SMEM_ACT_SCALES + NUM_BARS * 8 + SMEM_MISC;
   static_assert(SMEM_BYTES <= 232448, "more shared memory than one sm_100 CTA can have");
   static_assert(TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM allocation");
-  static_assert(STAGE_BYTES % 1024 == 0, "stages must stay 1024-byte aligned");
+  static_assert(STAGE_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "tiles must stay 1024-byte aligned");
 };
 
 enum WaitSite : uint32_t {
@@ -137,6 +144,7 @@ enum WaitSite : uint32_t {
   kWaitAccFull = 4,
   kWaitDrain = 5,
   kWaitMmaDone = 6,
+  kWaitActReady = 7,
 };
 
 struct UnitCoord {
@@ -177,10 +185,85 @@ __device__ __forceinline__ uint32_t bf16x2_bits(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&b);
 }
 
+// In-kernel quantization of one unit's activations (FUSE): the tokens
+// tok0 .. tok0 + BN - 1 over K blocks kt0 .. kt1 - 1 become the unit's
+// resident B operand (one [BN x 128 B] 128-byte-swizzled tile per K block
+// at s_act + k * B_BYTES) and scales (s_act_scales[k * BN + token]).  The
+// epilogue's threads share the work: a half-warp per (K block, token) group,
+// QB groups per half-warp with all their loads issued first.  Real tokens
+// get the quantization kernel's arithmetic (amax from eps, IEEE amax / 448,
+// clamp, round-to-nearest-even e4m3 with saturation); tokens past M get zero
+// codes and a zero scale without dividing (a zero row divided by an
+// eps-sized scale would take the division's slow path for nothing).
+template <class Cfg>
+__device__ __forceinline__ void quantize_unit(const GemmParams& p, const UnitCoord& c, uint32_t s_act,
+                                              uint32_t s_act_scales, int ethread) {
+  constexpr int BN = Cfg::BN, QB = 4;
+  constexpr int HALVES = Cfg::EPI_THREADS / 16;
+  const int lane16 = ethread & 15, half = ethread >> 4;
+  const int tok0 = c.tc * BN;
+  const int rows = min(BN, p.M - tok0);
+  const int groups = (c.kt1 - c.kt0) * BN;
+  // Every thread walks the same batches (the shuffle needs all 32 lanes);
+  // half-warp h takes groups g0 + h + b * HALVES of each batch.
+  for (int g0 = 0; g0 < groups; g0 += HALVES * QB) {
+    uint4 v[QB];
+#pragma unroll
+    for (int b = 0; b < QB; ++b) {
+      const int g = g0 + half + b * HALVES;
+      const int kl = g / BN, row = g % BN;
+      const int col = (c.kt0 + kl) * 128 + lane16 * 8;
+      v[b] = make_uint4(0u, 0u, 0u, 0u);
+      if (g < groups && row < rows && col < p.K)
+        v[b] = __ldg(reinterpret_cast<const uint4*>(p.x + int64_t(tok0 + row) * p.ldx + col));
+    }
+#pragma unroll
+    for (int b = 0; b < QB; ++b) {
+      const int g = g0 + half + b * HALVES;
+      const int kl = g / BN, row = g % BN;
+      const bool real = g < groups && row < rows;
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v[b]);
+      float f[8];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 t = __bfloat1622float2(h[e]);
+        f[2 * e] = t.x;
+        f[2 * e + 1] = t.y;
+      }
+      float amax = p.eps;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(f[e]));
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      if (g >= groups) continue;
+      uint32_t packed[2] = {0u, 0u};
+      float scale = 0.f;
+      if (real) {
+        scale = amax / 448.f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 q = make_float2(fminf(fmaxf(f[2 * e] / scale, -448.f), 448.f),
+                                       fminf(fmaxf(f[2 * e + 1] / scale, -448.f), 448.f));
+          const uint32_t pair = __nv_cvt_float2_to_fp8x2(q, __NV_SATFINITE, __NV_E4M3);
+          packed[e >> 1] |= pair << (16 * (e & 1));
+        }
+      }
+      // 8 codes of chunk lane16 of token row `row`: 16-byte unit lane16 / 2
+      // of the row, XOR-swizzled with the row inside its 8-row group.
+      const uint32_t unit16 = uint32_t(lane16 >> 1) ^ uint32_t(row & 7);
+      st_shared_v2(s_act + uint32_t(kl) * Cfg::B_BYTES + uint32_t(row) * 128u + unit16 * 16u +
+                       uint32_t(lane16 & 1) * 8u,
+                   packed[0], packed[1]);
+      if (lane16 == 0) st_shared_f32(s_act_scales + uint32_t(kl * BN + row) * 4u, scale);
+    }
+  }
+  fence_proxy_async_smem();  // the MMAs read the operand through the async proxy
+}
+
 template <class Cfg>
 __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_constant__ GemmParams p) {
   constexpr int BN = Cfg::BN, STAGES = Cfg::STAGES, ACC_BUFS = Cfg::ACC_BUFS, COLS = Cfg::COLS;
-  constexpr bool SWAP = Cfg::SWAP;
+  constexpr bool SWAP = Cfg::SWAP, FUSE = Cfg::FUSE;
   constexpr int PF = 4;  // scale prefetch distance in K blocks
 
   extern __shared__ uint8_t smem_raw[];
@@ -188,18 +271,17 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
   const uint32_t base = (raw + 1023u) & ~1023u;  // swizzled tiles need 1024-byte alignment
   uint8_t* smem = smem_raw + (base - raw);
   const uint32_t s_tiles = base;
-  const uint32_t s_out = base + Cfg::SMEM_TILES;
-  const uint32_t s_scales = s_out + Cfg::SMEM_OUT;  // FUSE: [ACC_BUFS][BN] fp32
-  const uint32_t s_bars = s_scales + Cfg::SMEM_SCALES;
+  const uint32_t s_act = s_tiles + Cfg::SMEM_TILES;  // FUSE: the unit's B operand
+  const uint32_t s_out = s_act + Cfg::SMEM_ACT;
+  const uint32_t s_act_scales = s_out + Cfg::SMEM_OUT;  // FUSE: [ACT_KB][BN] fp32
+  const uint32_t s_bars = s_act_scales + Cfg::SMEM_ACT_SCALES;
   auto full = [&](int s) { return s_bars + 8u * s; };
   auto empty = [&](int s) { return s_bars + 8u * (STAGES + s); };
   auto acc_full = [&](int a) { return s_bars + 8u * (2 * STAGES + a); };
   auto acc_empty = [&](int a) { return s_bars + 8u * (2 * STAGES + ACC_BUFS + a); };
   const uint32_t mma_done = s_bars + 8u * (2 * STAGES + 2 * ACC_BUFS);
-  auto xfull = [&](int s) { return s_bars + 8u * (2 * STAGES + 2 * ACC_BUFS + 1 + s); };
-  auto scale_ready = [&](int a) { return s_bars + 8u * (3 * STAGES + 2 * ACC_BUFS + 1 + a); };
-  uint32_t* misc = reinterpret_cast<uint32_t*>(smem + Cfg::SMEM_TILES + Cfg::SMEM_OUT + Cfg::SMEM_SCALES +
-                                               8 * Cfg::NUM_BARS);
+  const uint32_t act_ready = s_bars + 8u * (2 * STAGES + 2 * ACC_BUFS + 1);
+  uint32_t* misc = reinterpret_cast<uint32_t*>(smem + (s_bars - base) + 8 * Cfg::NUM_BARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 1);
   volatile int* last_flag = reinterpret_cast<volatile int*>(misc + 2);
   volatile int* stage_seq = reinterpret_cast<volatile int*>(misc + 4);  // last K block loaded per stage
@@ -208,26 +290,23 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(full(s), Cfg::FUSE ? 2 : 1);  // FUSE: the weight TMA + the quantizer warp
+      mbar_init(full(s), 1);
       mbar_init(empty(s), 1);
-      if constexpr (Cfg::FUSE) mbar_init(xfull(s), 1);
     }
-    if constexpr (Cfg::FUSE)
-      for (int a = 0; a < ACC_BUFS; ++a) mbar_init(scale_ready(a), 1);
     for (int a = 0; a < ACC_BUFS; ++a) {
       mbar_init(acc_full(a), 1);
       mbar_init(acc_empty(a), Cfg::EPI_WARPS);
     }
-    mbar_init(mma_done, 2);  // one commit from each MMA issuer
+    mbar_init(mma_done, 2);   // one commit from each MMA issuer
+    mbar_init(act_ready, 1);  // FUSE: a unit's quantized activations are in place
     *abort_flag = 0;
     for (int st = 0; st < STAGES; ++st) stage_seq[st] = -1;
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&p.map_a);
-    tma_prefetch_desc(&p.map_b);
+    if constexpr (!FUSE) tma_prefetch_desc(&p.map_b);
     tma_prefetch_desc(&p.map_c);
-    if constexpr (Cfg::FUSE) tma_prefetch_desc(&p.map_x);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(misc), Cfg::TMEM_COLS);
@@ -246,140 +325,54 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
     // two threads in parallel.  K block i of the sequence always uses smem
     // stage i % STAGES (phase (i / STAGES) & 1) and TMEM buffer i % ACC_BUFS
     // (phase (i / ACC_BUFS) & 1), whoever handles it.
-    // FUSE: warp 0 is the only producer (weights + bf16 activation tiles
-    // for every K block) and warp 3 the quantizer warp.
-    const bool producer = Cfg::FUSE ? warp == 0 : (warp == 0 || warp == 3);
-    const bool quantizer = Cfg::FUSE && warp == 3;
+    const bool producer = warp == 0 || warp == 3;
     const int role = (warp == 0 || warp == 1) ? 0 : 1;  // which half of the K blocks
-    auto mine = [&](int seq) { return ((Cfg::FUSE && producer) || (seq & 1) == role); };
-    if (quantizer) {
-      if constexpr (Cfg::FUSE) {
-        // ------------------------------------------------------------ quantizer warp
-        // Per K block: the bf16 tile [BN tokens x 128] staged by TMA becomes
-        // the e4m3 B operand in the 128-byte swizzle the MMA expects, and
-        // each token's scale goes to the scale slot of the block's TMEM
-        // buffer.  Same arithmetic as quantize_kernel: amax from eps, IEEE
-        // amax / 448, clamp, round-to-nearest-even e4m3 with saturation.
-        // Rows past M and columns past K were zero-filled by the TMA, so they
-        // quantize to zero codes.
-        constexpr int LPR = BN >= 32 ? 1 : 32 / BN;  // lanes per token row
-        constexpr int RPL = BN >= 32 ? BN / 32 : 1;  // token rows per lane
-        constexpr int CPL = 16 / LPR;                // 16-byte bf16 chunks per lane per row
-        int seq = 0;
-        bool ok = true;
-        for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
-          const UnitCoord c = unit_coord(p, u);
-          for (int kt = c.kt0; kt < c.kt1; ++kt, ++seq) {
-            const int stage = seq % STAGES, slot = seq % ACC_BUFS;
-            if (!mbar_wait(xfull(stage), uint32_t(seq / STAGES) & 1u, abort_flag, kWaitFull) ||
-                !mbar_wait(acc_empty(slot), (uint32_t(seq / ACC_BUFS) & 1u) ^ 1u, abort_flag,
-                           kWaitAccEmpty)) {
-              ok = false;
-              break;
-            }
-            const uint32_t st_base = s_tiles + uint32_t(stage) * Cfg::STAGE_BYTES;
-            const uint32_t b_tile = st_base + Cfg::A_BYTES;
-            const uint32_t x_tile = b_tile + Cfg::B_BYTES;
-#pragma unroll
-            for (int rr = 0; rr < RPL; ++rr) {
-              const int row = lane / LPR + rr * (32 / LPR);
-              const int part = lane % LPR;
-              uint4 v[CPL];
-#pragma unroll
-              for (int j = 0; j < CPL; ++j) {  // rotated start: 4 wavefronts per load
-                const int ch = part * CPL + ((j + lane) % CPL);
-                v[j] = ld_shared_v4(x_tile + uint32_t(row) * 256u + uint32_t(ch) * 16u);
-              }
-              float amax = p.eps;
-#pragma unroll
-              for (int j = 0; j < CPL; ++j) {
-                const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v[j]);
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  const float2 f = __bfloat1622float2(h[e]);
-                  amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
-                }
-              }
-#pragma unroll
-              for (int o = LPR / 2; o > 0; o >>= 1)
-                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-              const float scale = amax / 448.f;
-#pragma unroll
-              for (int j = 0; j < CPL; ++j) {
-                const int ch = part * CPL + ((j + lane) % CPL);  // 8 values -> 8 e4m3 bytes
-                const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v[j]);
-                uint32_t packed[2] = {0u, 0u};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  const float2 f = __bfloat1622float2(h[e]);
-                  const float2 q = make_float2(fminf(fmaxf(f.x / scale, -448.f), 448.f),
-                                               fminf(fmaxf(f.y / scale, -448.f), 448.f));
-                  const uint32_t pair = __nv_cvt_float2_to_fp8x2(q, __NV_SATFINITE, __NV_E4M3);
-                  packed[e >> 1] |= pair << (16 * (e & 1));
-                }
-                const uint32_t unit16 = uint32_t(ch >> 1) ^ uint32_t(row & 7);  // 128-byte swizzle
-                st_shared_v2(b_tile + uint32_t(row) * 128u + unit16 * 16u + uint32_t(ch & 1) * 8u,
-                             packed[0], packed[1]);
-              }
-              if (part == 0) st_shared_f32(s_scales + uint32_t(slot * BN + row) * 4u, scale);
-            }
-            fence_proxy_async_smem();  // the MMA reads the B tile through the async proxy
-            __syncwarp();
-            if (lane == 0) {
-              mbar_arrive(full(stage));
-              mbar_arrive(scale_ready(slot));
-            }
-          }
-        }
-      }
-    } else if (lane == 0) {
+    if (lane == 0) {
       if (producer) {
         // ------------------------------------------------------------ TMA producer
         // Activations are re-read by many tiles: keep them; weights streamed
         // once (decode) go first.
         const uint64_t pol_act = policy_evict_last();
         const uint64_t pol_wgt = p.stream_b ? policy_evict_first() : policy_evict_normal();
-        const uint64_t pol_a = SWAP ? pol_wgt : pol_act;
-        const uint64_t pol_b = SWAP ? pol_act : pol_wgt;
         // Weights are operand A when swapped, B otherwise.  After our own
         // quantizer (p.pdl, programmatic dependent launch) the weight tiles
         // of this thread's first K blocks (among the first STAGES) go out
         // before griddepcontrol.wait, so they stream while the quantizer
-        // finishes; activation tiles only after it.
+        // finishes; activation tiles only after it.  FUSE: the ring carries
+        // weight tiles only.
         const CUtensorMap* map_w = SWAP ? &p.map_a : &p.map_b;
         const CUtensorMap* map_x = SWAP ? &p.map_b : &p.map_a;
         const uint32_t off_w = SWAP ? 0u : uint32_t(Cfg::A_BYTES);
         const uint32_t off_x = SWAP ? uint32_t(Cfg::A_BYTES) : 0u;
-        const uint64_t pol_w = SWAP ? pol_a : pol_b;
-        const uint64_t pol_x = SWAP ? pol_b : pol_a;
+        constexpr uint32_t kFullBytes = Cfg::STAGE_BYTES;
         auto w_row = [&](const UnitCoord& c) { return SWAP ? c.tr * 128 : c.tc * BN; };
         auto x_row = [&](const UnitCoord& c) { return SWAP ? c.tc * BN : c.tr * 128; };
         int early = 0;  // K blocks (of the whole sequence) whose weights went out early
-        if (p.pdl) {
+        if (p.pdl && !FUSE) {
           int seq = 0;
           for (int u = blockIdx.x; u < p.units && seq < STAGES; u += gridDim.x) {
             const UnitCoord c = unit_coord(p, u);
             for (int kt = c.kt0; kt < c.kt1 && seq < STAGES; ++kt, ++seq) {
-              if (!mine(seq)) continue;
+              if ((seq & 1) != role) continue;
               const uint32_t dst = s_tiles + uint32_t(seq) * Cfg::STAGE_BYTES;  // stage = seq
-              mbar_arrive_expect_tx(full(seq), Cfg::FULL_TX);
-              tma_load_2d(dst + off_w, map_w, kt * 128, w_row(c), full(seq), pol_w);
+              mbar_arrive_expect_tx(full(seq), kFullBytes);
+              tma_load_2d(dst + off_w, map_w, kt * 128, w_row(c), full(seq), pol_wgt);
               stage_seq[seq] = seq;
             }
           }
           early = seq;
         }
-        griddep_wait();  // activations are the previous kernel's output
+        if (!FUSE) griddep_wait();  // activations are the previous kernel's output
         int seq = 0;
         bool ok = true;
         for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
           const UnitCoord c = unit_coord(p, u);
           for (int kt = c.kt0; kt < c.kt1; ++kt, ++seq) {
-            if (!mine(seq)) continue;
+            if ((seq & 1) != role) continue;
             const int stage = seq % STAGES;
             const uint32_t dst = s_tiles + uint32_t(stage) * Cfg::STAGE_BYTES;
             if (seq < early) {  // weights already requested; add the activations
-              tma_load_2d(dst + off_x, map_x, kt * 128, x_row(c), full(stage), pol_x);
+              tma_load_2d(dst + off_x, map_x, kt * 128, x_row(c), full(stage), pol_act);
               continue;
             }
             const uint32_t phase = uint32_t(seq / STAGES) & 1u;
@@ -387,30 +380,25 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
               ok = false;
               break;
             }
-            mbar_arrive_expect_tx(full(stage), Cfg::FULL_TX);
-            tma_load_2d(dst + off_w, map_w, kt * 128, w_row(c), full(stage), pol_w);
-            if constexpr (Cfg::FUSE) {  // bf16 activations into the stage's staging area
-              mbar_arrive_expect_tx(xfull(stage), Cfg::X_BYTES);
-              tma_load_2d(dst + Cfg::A_BYTES + Cfg::B_BYTES, &p.map_x, kt * 128, c.tc * BN, xfull(stage),
-                          pol_x);
-            } else {
-              tma_load_2d(dst + off_x, map_x, kt * 128, x_row(c), full(stage), pol_x);
-            }
+            mbar_arrive_expect_tx(full(stage), kFullBytes);
+            tma_load_2d(dst + off_w, map_w, kt * 128, w_row(c), full(stage), pol_wgt);
+            if constexpr (!FUSE) tma_load_2d(dst + off_x, map_x, kt * 128, x_row(c), full(stage), pol_act);
             stage_seq[stage] = seq;
           }
         }
       } else {
         // ------------------------------------------------------------ MMA issuer
         constexpr uint32_t idesc = idesc_e4m3_f32(128, BN);
-        // Descriptors of stage 0's tiles; a stage or a K step only moves the
-        // 14-bit start-address field (16-byte units), which never carries out
-        // (shared memory ends below 256 KB).
+        // Descriptors of stage 0's tiles; a stage, a resident K block or a K
+        // step only moves the 14-bit start-address field (16-byte units),
+        // which never carries out (shared memory ends below 256 KB).
         const uint64_t desc_a0 = smem_desc_k128_sw128(s_tiles);
-        const uint64_t desc_b0 = smem_desc_k128_sw128(s_tiles + Cfg::A_BYTES);
-        int seq = 0;
+        const uint64_t desc_b0 = smem_desc_k128_sw128(FUSE ? s_act : s_tiles + Cfg::A_BYTES);
+        int seq = 0, unit_no = 0;
         bool ok = true;
-        for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
+        for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x, ++unit_no) {
           const UnitCoord c = unit_coord(p, u);
+          if (FUSE && !mbar_wait(act_ready, uint32_t(unit_no) & 1u, abort_flag, kWaitActReady)) break;
           for (int kt = c.kt0; kt < c.kt1; ++kt, ++seq) {
             if ((seq & 1) != role) continue;
             const int stage = seq % STAGES, acc = seq % ACC_BUFS;
@@ -422,11 +410,12 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
               break;
             }
             tc_fence_after();
-            const uint64_t stage_off = uint64_t(stage) * (Cfg::STAGE_BYTES >> 4);
+            const uint64_t a_off = uint64_t(stage) * (Cfg::STAGE_BYTES >> 4);
+            const uint64_t b_off = FUSE ? uint64_t(kt - c.kt0) * (Cfg::B_BYTES >> 4) : a_off;
             const uint32_t d = tmem_base + uint32_t(acc * BN);
 #pragma unroll
             for (int k = 0; k < 4; ++k)  // K step of 32 e4m3 = 32 bytes = 2 descriptor units
-              mma_f8(d, desc_a0 + stage_off + 2 * k, desc_b0 + stage_off + 2 * k, idesc, k > 0 ? 1u : 0u);
+              mma_f8(d, desc_a0 + a_off + 2 * k, desc_b0 + b_off + 2 * k, idesc, k > 0 ? 1u : 0u);
             mma_commit(empty(stage));   // the smem stage is free once these MMAs are done
             mma_commit(acc_full(acc));  // ... and the partial sums are in TMEM
           }
@@ -437,18 +426,15 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
       }
     }
     __syncwarp();  // reconverge before the barriers below (bar.sync is .aligned)
-    if (warp == 0 || warp == 3) {
+    if (producer) {
       // Every issued copy must land before the CTA exits.  On the normal path
       // the MMA threads have seen them all; after an abort, wait on the last
       // load of each stage (its phase completes when its bytes arrive).
-      named_bar_sync(2, 64);  // warps 0 and 3 are done issuing (and quantizing)
+      named_bar_sync(2, 64);  // both producers are done issuing
       if (warp == 0 && lane == 0)
         for (int st = 0; st < STAGES; ++st)
-          if (stage_seq[st] >= 0) {
-            const uint32_t ph = uint32_t(stage_seq[st] / STAGES) & 1u;
-            if constexpr (Cfg::FUSE) mbar_wait(xfull(st), ph, nullptr, kWaitDrain);
-            mbar_wait(full(st), ph, nullptr, kWaitDrain);
-          }
+          if (stage_seq[st] >= 0)
+            mbar_wait(full(st), uint32_t(stage_seq[st] / STAGES) & 1u, nullptr, kWaitDrain);
       __syncwarp();
     }
   } else {
@@ -469,7 +455,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
     // Scale sources of a unit.  Normal: sa per row (thread), sb per
     // 128-column block (warpgroup).  Swapped: sb per 128-row tile (CTA), sa
     // per token column; lane j loads token col0 + j (and col0 + 32 + j when
-    // BN = 64).
+    // BN = 64).  FUSE: sa comes from the unit's resident scales.
     struct ScaleSrc {
       const float* sa;
       const float* sa2;
@@ -487,10 +473,10 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
         q.sb = p.sb + int64_t(q.sb_ok ? col0 / 128 : 0) * p.sb_n;
       } else {
         const int t0 = col0 + lane, t1 = col0 + 32 + lane;
-        q.sa_ok = !Cfg::FUSE && t0 < p.M && lane < BN;  // FUSE: scales come from smem
+        q.sa_ok = !FUSE && t0 < p.M && lane < BN;
         q.sa = p.sa + int64_t(q.sa_ok ? t0 : 0) * p.sa_m;
         if constexpr (BN > 32) {
-          q.sa2_ok = !Cfg::FUSE && t1 < p.M;
+          q.sa2_ok = !FUSE && t1 < p.M;
           q.sa2 = p.sa + int64_t(q.sa2_ok ? t1 : 0) * p.sa_m;
         }
         q.sb_ok = true;  // the tile's weight block exists (tr * 128 < N)
@@ -510,11 +496,22 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
       for (int j = 0; j < PF; ++j)
         if (c.kt0 + j < c.kt1) load_scales(q, c.kt0 + j, j);
     };
+    // FUSE: quantize a unit's activations, then hand them to the MMA issuers.
+    auto publish_unit = [&](const UnitCoord& c) {
+      if constexpr (FUSE) {
+        quantize_unit<Cfg>(p, c, s_act, s_act_scales, ew * 32 + lane);
+        named_bar_sync(1, Cfg::EPI_THREADS);
+        if (ew == 0 && lane == 0) mbar_arrive(act_ready);
+      }
+    };
 
-    griddep_wait();  // activation scales are the previous kernel's output
+    if (!FUSE) griddep_wait();  // activation scales are the previous kernel's output
     UnitCoord c_next = unit_coord(p, blockIdx.x < p.units ? blockIdx.x : 0);
     ScaleSrc src_next = scale_src(c_next);
-    if (blockIdx.x < p.units) prefetch_unit(src_next, c_next);
+    if (blockIdx.x < p.units) {
+      prefetch_unit(src_next, c_next);
+      publish_unit(c_next);
+    }
 
     for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
       const UnitCoord c = c_next;
@@ -536,18 +533,17 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
         for (int j = 0; j < PF; ++j) {
           const int kt = kt_base + j;
           if (kt < c.kt1) {
-            const float sa_v = pa[j], sb_v = pb[j];
+            float sa_v = pa[j], sb_v = pb[j];
             float sa2_v = 0.f;
             if constexpr (SWAP && BN > 32) sa2_v = pa2[j];
             if (kt + PF < c.kt1) load_scales(src, kt + PF, j);
+            if constexpr (FUSE) {  // the token scales quantize_unit wrote for this K block
+              const uint32_t sl = s_act_scales + uint32_t((kt - c.kt0) * BN) * 4u;
+              sa_v = lane < BN ? ld_shared_f32(sl + uint32_t(lane) * 4u) : 0.f;
+              if constexpr (BN > 32) sa2_v = ld_shared_f32(sl + uint32_t(32 + lane) * 4u);
+            }
             ok = mbar_wait(acc_full(acc), acc_phase, abort_flag, kWaitAccFull) && ok;
             tc_fence_after();
-            float sa_f = sa_v, sa2_f = sa2_v;
-            if constexpr (Cfg::FUSE) {  // this K block's token scales, from the quantizer warp
-              ok = mbar_wait(scale_ready(acc), acc_phase, abort_flag, kWaitAccFull) && ok;
-              sa_f = lane < BN ? ld_shared_f32(s_scales + uint32_t(acc * BN + lane) * 4u) : 0.f;
-              if constexpr (BN > 32) sa2_f = ld_shared_f32(s_scales + uint32_t(acc * BN + 32 + lane) * 4u);
-            }
             if (work) {
               const uint32_t t = t_lane + uint32_t(acc * BN + g * COLS);
               if constexpr (!SWAP) {
@@ -566,10 +562,10 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
                 for (int ch = 0; ch < BN / CH; ++ch) {
                   float part[CH];
                   tmem_ld<CH>(t + CH * ch, part);
-                  const float src = ch == 0 ? sa_f : sa2_f;
+                  const float src_s = ch == 0 ? sa_v : sa2_v;
 #pragma unroll
                   for (int i = 0; i < CH; ++i) {
-                    const float scale = __shfl_sync(0xffffffffu, src, i) * sb_v;
+                    const float scale = __shfl_sync(0xffffffffu, src_s, i) * sb_v;
                     accum[CH * ch + i] = fmaf(part[i], scale, accum[CH * ch + i]);
                   }
                 }
@@ -587,11 +583,17 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
       }
 
       // The next unit's first scales go out now, ahead of this unit's
-      // split-K hand-off and store.
+      // split-K hand-off and store; FUSE also quantizes the next unit here
+      // (all of this unit's MMAs are done: every K block's partial has been
+      // read, and every epilogue thread is past its scales).
       if (u + int(gridDim.x) < p.units) {
         c_next = unit_coord(p, u + gridDim.x);
         src_next = scale_src(c_next);
         prefetch_unit(src_next, c_next);
+        if constexpr (FUSE) {
+          named_bar_sync(1, Cfg::EPI_THREADS);
+          publish_unit(c_next);
+        }
       }
 
       bool store = work;
