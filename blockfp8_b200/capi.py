@@ -57,17 +57,23 @@ def launch_gemm(p: GemmProblem, plan: Plan, workspace=None, counters=None, strea
                                           _stream(stream)))
 
 
-def gemm(a, a_scales, b, b_scales, config: int = -1, splits: int = 0, fused: bool = False,
+def gemm(a, a_scales, b, b_scales, config: int = -1, splits: int = 0, fused=False,
          eps: float = 1e-10, stream=None) -> torch.Tensor:
-    """C = block-scaled A @ B^T through the C ABI alone (A bf16 when fused)."""
+    """C = block-scaled A @ B^T through the C ABI alone (A bf16 when fused).
+
+    fused: False (A is e4m3 with a_scales), True (bf16 A, the library's
+    fused plan), or a bfp8_plan.fused mode (1: quantization kernel + GEMM,
+    2: quantization inside the GEMM where the plan allows it)."""
     c = torch.empty(a.shape[0], b.shape[0], dtype=torch.bfloat16, device=a.device)
     p = problem(a, a_scales, b, b_scales, c, eps)
     sms = torch.cuda.get_device_properties(a.device).multi_processor_count
-    plan = choose_plan(p.M, p.N, p.K, sms, fused)
+    plan = choose_plan(p.M, p.N, p.K, sms, bool(fused))
     if config >= 0:
-        plan.config, plan.splits = config, max(1, splits)
-    elif splits > 0:
-        plan.splits = splits
+        plan.config, plan.splits = config, splits if splits != 0 else 1
+    elif splits != 0:
+        plan.splits = splits  # < 0: stream-K over -splits CTAs
+    if fused is not True and fused is not False:
+        plan.fused = int(fused)
     ws, cnt = scratch(p, plan, a.device)
     launch_gemm(p, plan, ws, cnt, stream)
     return c

@@ -99,8 +99,8 @@ using CfgW32 = GemmCfg<32, 10, true>;
 using CfgW64 = GemmCfg<64, 8, true>;
 // ... quantizing in the kernel: the unit's B operand is resident (64 KB),
 // the ring carries only weight tiles
-using CfgW16Q = GemmCfg<16, 9, true, true>;
-using CfgW32Q = GemmCfg<32, 9, true, true>;
+using CfgW16Q = GemmCfg<16, 8, true, true>;
+using CfgW32Q = GemmCfg<32, 8, true, true>;
 using CfgW64Q = GemmCfg<64, 8, true, true>;
 
 const ConfigEntry kConfigs[] = {
@@ -156,17 +156,25 @@ int ensure_smem_attr(int config, int dev, bool in_kernel_quant) {
   return BFP8_OK;
 }
 
+// A plan's shape.  Round-robin split-K: `splits` parts of k_per_split K
+// blocks per tile.  Stream-K (plan.splits < 0): sk_grid CTAs share the
+// sk_work = tiles * k_tiles K blocks evenly; k_per_split is then the longest
+// unit and `splits` the most parts any tile is cut into.
 struct Derived {
   int tiles_r, tiles_c, tiles, k_tiles, k_per_split, splits;
+  int sk_grid = 0;
+  int64_t sk_work = 0;
 };
 Derived derive(const bfp8_gemm_problem& p, const bfp8_plan& plan);
 
-// Fused plans of swapped configurations whose units fit the resident operand
-// quantize inside the GEMM kernel; the others run the quantization kernel
-// into the workspace first (same results either way).
+// Plans that ask for quantization inside the GEMM, of swapped configurations
+// whose units fit the resident operand, quantize in the GEMM kernel; other
+// fused plans run the quantization kernel into the workspace first (same
+// results either way).
 bool quantizes_in_kernel(const bfp8_gemm_problem& p, const bfp8_plan& plan) {
   const ConfigEntry& e = kConfigs[plan.config];
-  return plan.fused && e.launch_fused != nullptr && derive(p, plan).k_per_split <= e.act_kb;
+  return plan.fused == BFP8_FUSED_IN_GEMM && e.launch_fused != nullptr &&
+         derive(p, plan).k_per_split <= e.act_kb;
 }
 
 // ---- tensor maps --------------------------------------------------------------------
@@ -212,6 +220,17 @@ const TableEntry kPlanTable[] = {
     {0, 0, 0, 0, 0}};
 constexpr int kPlanEntries = int(sizeof(kPlanTable) / sizeof(kPlanTable[0])) - 1;
 
+// Fused plans (bf16 in): the faster of quantization kernel + GEMM and
+// quantization inside the GEMM, with its own configuration and splits,
+// where the sweep timed both (decode sizes).
+struct FusedTableEntry {
+  int n, k, m, config, splits, mode;
+};
+const FusedTableEntry kFusedPlanTable[] = {
+#include "fused_plan_table.inc"
+    {0, 0, 0, 0, 0, 0}};
+constexpr int kFusedPlanEntries = int(sizeof(kFusedPlanTable) / sizeof(kFusedPlanTable[0])) - 1;
+
 // The entry for this (N, K) with the smallest tabulated M >= M, else the
 // largest (the reference's lookup rule, csrc/gemm_sm89.cu:158-169).
 template <class E>
@@ -232,17 +251,32 @@ const E* lookup(const E* table, int n_entries, int M, int N, int K) {
 // runs ceil(units / SMs) units of k_per_split K blocks; a K block costs the
 // larger of its MMA time (4 MMAs of 128 x BN x 32 at 8192 e4m3 MACs per SM
 // clock) and its operand bytes at the SM's share of HBM bandwidth; split-K
-// adds the fp32 partial round trip of the valid rows.
+// adds the fp32 partial round trip of the valid rows.  Stream-K (splits < 0)
+// is one wave of -splits CTAs with ceil(W / CTAs) K blocks each and up to
+// two units (and partial round trips) per CTA.
 double plan_cost_ns(int M, int N, int K, int num_sms, int config, int splits) {
   const ConfigEntry& e = kConfigs[config];
   const int k_tiles = cdiv(K, 128);
-  const int per = cdiv(k_tiles, std::max(1, std::min(splits, k_tiles)));
-  const int real_splits = cdiv(k_tiles, per);
   const int rows_total = e.swap ? N : M, cols_total = e.swap ? M : N;
   const int tiles_r = cdiv(rows_total, 128), tiles_c = cdiv(cols_total, e.bn);
-  const int64_t units = int64_t(tiles_r) * tiles_c * real_splits;
-  const int64_t waves = (units + num_sms - 1) / num_sms;
-  const int active = int(std::min<int64_t>(units, num_sms));
+  int per, real_splits;
+  int64_t waves;
+  int active;
+  if (splits < 0) {
+    const int64_t work = int64_t(tiles_r) * tiles_c * k_tiles;
+    const int64_t g = std::max<int64_t>(1, std::min<int64_t>(-int64_t(splits), work));
+    per = int((work + g - 1) / g);
+    real_splits = per < k_tiles ? 2 : 1;  // a partial round trip in most units
+    waves = per < k_tiles ? 2 : (per + k_tiles - 1) / k_tiles;  // units per CTA
+    active = int(g);
+    per = int((work + g - 1) / g / waves);  // K blocks per unit, on average
+  } else {
+    per = cdiv(k_tiles, std::max(1, std::min(splits, k_tiles)));
+    real_splits = cdiv(k_tiles, per);
+    const int64_t units = int64_t(tiles_r) * tiles_c * real_splits;
+    waves = (units + num_sms - 1) / num_sms;
+    active = int(std::min<int64_t>(units, num_sms));
+  }
   const double clk_ghz = 1.8;
   const double mma_ns = 2.0 * e.bn / clk_ghz;
   const int rows = std::min(rows_total, 128);
@@ -265,7 +299,15 @@ bfp8_plan heuristic_plan(int M, int N, int K, int num_sms, bool fused) {
   double best_t = 1e300;
   const int k_tiles = cdiv(K, 128);
   for (int config = 0; config < kNumConfigs; ++config) {
-    for (int splits = 1; splits <= std::min(k_tiles, 16); ++splits) {
+    for (int splits = 0; splits <= std::min(k_tiles, 16); ++splits) {
+      if (splits == 0) {  // stream-K over every SM
+        const double t = plan_cost_ns(M, N, K, num_sms, config, -num_sms);
+        if (t < best_t * 0.999) {
+          best_t = t;
+          best = {config, -num_sms, fused ? 1 : 0};
+        }
+        continue;
+      }
       const int per = cdiv(k_tiles, splits);
       if (cdiv(k_tiles, per) != splits) continue;  // same as a smaller split count
       const double t = plan_cost_ns(M, N, K, num_sms, config, splits);
@@ -306,6 +348,23 @@ Derived derive(const bfp8_gemm_problem& p, const bfp8_plan& plan) {
   d.tiles_c = cdiv(e.swap ? p.M : p.N, e.bn);
   d.tiles = d.tiles_r * d.tiles_c;
   d.k_tiles = cdiv(p.K, 128);
+  if (plan.splits < 0) {
+    // Stream-K: CTA b takes K-block positions [W b / G, W (b + 1) / G); the
+    // CTAs starting at or before position x number min(G, ceil((x + 1) G / W)).
+    const int64_t W = int64_t(d.tiles) * d.k_tiles;
+    const int64_t G = std::max<int64_t>(1, std::min<int64_t>(-int64_t(plan.splits), W));
+    d.sk_grid = int(G);
+    d.sk_work = W;
+    d.k_per_split = int(std::min<int64_t>(d.k_tiles, (W + G - 1) / G));
+    auto starts_upto = [&](int64_t x) { return std::min<int64_t>(G, ((x + 1) * G + W - 1) / W); };
+    int most = 1;
+    for (int t = 0; t < d.tiles; ++t) {
+      const int64_t t0 = int64_t(t) * d.k_tiles;
+      most = std::max(most, int(starts_upto(t0 + d.k_tiles - 1) - starts_upto(t0) + 1));
+    }
+    d.splits = most;
+    return d;
+  }
   const int splits = std::max(1, std::min(plan.splits, d.k_tiles));
   d.k_per_split = cdiv(d.k_tiles, splits);
   d.splits = cdiv(d.k_tiles, d.k_per_split);  // no empty splits
@@ -407,13 +466,17 @@ bfp8_plan bfp8_choose_plan(int M, int N, int K, int num_sms) {
   return heuristic_plan(M, N, K, num_sms, false);
 }
 
-// The fused path is the quantization kernel followed by the same GEMM
-// kernels, launched with programmatic dependent launch so the GEMM's
-// prologue and first weight loads overlap the quantizer; it takes the same
-// plan as the unfused GEMM.
+// The fused path runs either the quantization kernel followed by the GEMM,
+// launched with programmatic dependent launch so the GEMM's prologue and
+// first weight loads overlap the quantizer (the unfused GEMM's plan), or a
+// GEMM that quantizes its own activations; the fused table says which is
+// faster where both were timed, up to its largest M for the shape.
 bfp8_plan bfp8_choose_fused_plan(int M, int N, int K, int num_sms) {
+  if (const FusedTableEntry* t = lookup(kFusedPlanTable, kFusedPlanEntries, M, N, K))
+    if (t->m >= M && (t->mode == BFP8_FUSED_QUANT_KERNEL || t->mode == BFP8_FUSED_IN_GEMM))
+      return {t->config, t->splits, t->mode};
   bfp8_plan plan = bfp8_choose_plan(M, N, K, num_sms);
-  plan.fused = 1;
+  plan.fused = BFP8_FUSED_QUANT_KERNEL;
   return plan;
 }
 
@@ -465,7 +528,7 @@ int bfp8_launch_gemm(const bfp8_gemm_problem* pp, bfp8_plan plan, float* workspa
                      void* stream_) {
   if (!pp) return fail(BFP8_EINVAL, "null problem");
   if (!config_ok(plan.config)) return fail(BFP8_EINVAL, "config out of range");
-  if (plan.splits < 1) return fail(BFP8_EINVAL, "splits must be >= 1");
+  if (plan.splits == 0) return fail(BFP8_EINVAL, "splits must be >= 1 (or negative: stream-K)");
   bfp8_gemm_problem p = *pp;
   const bool fused = plan.fused != 0;
   if (int r = check_problem(p, fused)) return r;
@@ -547,7 +610,9 @@ int bfp8_launch_gemm(const bfp8_gemm_problem* pp, bfp8_plan plan, float* workspa
   gp.k_tiles = d.k_tiles;
   gp.k_per_split = d.k_per_split;
   gp.splits = d.splits;
-  gp.units = d.tiles * d.splits;
+  gp.units = d.sk_grid > 0 ? int(d.sk_work) : d.tiles * d.splits;
+  gp.sk_grid = d.sk_grid;
+  gp.sk_work = d.sk_work;
   // Raster: when all row tiles of the MMA A operand fit comfortably in L2,
   // sweep them all for each column tile, so A stays resident and B streams
   // from HBM once; otherwise groups of 8 row tiles (the reference's
@@ -558,7 +623,7 @@ int bfp8_launch_gemm(const bfp8_gemm_problem* pp, bfp8_plan plan, float* workspa
   gp.pdl = fused && !in_kernel ? 1 : 0;
 
   if (int r = ensure_smem_attr(plan.config, dev, in_kernel)) return r;
-  const int grid = std::min(gp.units, sms);
+  const int grid = d.sk_grid > 0 ? d.sk_grid : std::min(gp.units, sms);
   (in_kernel ? e.launch_fused : e.launch)(gp, grid, stream);
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return cuda_fail(err, "GEMM kernel launch");
@@ -568,7 +633,7 @@ int bfp8_launch_gemm(const bfp8_gemm_problem* pp, bfp8_plan plan, float* workspa
 int bfp8_launch_gemm_noalloc(const bfp8_gemm_problem* p, bfp8_plan plan, void* stream) {
   if (!p) return fail(BFP8_EINVAL, "null problem");
   if (!config_ok(plan.config)) return fail(BFP8_EINVAL, "config out of range");
-  if (plan.splits < 1) return fail(BFP8_EINVAL, "splits must be >= 1");
+  if (plan.splits == 0) return fail(BFP8_EINVAL, "splits must be >= 1 (or negative: stream-K)");
   if (p->M <= 0) return bfp8_launch_gemm(p, plan, nullptr, nullptr, stream);
   const int64_t ws = bfp8_workspace_bytes(p, plan);
   const int counters = bfp8_counters_needed(p, plan);

@@ -75,7 +75,9 @@ struct GemmParams {
   int M, N, K;
   int tiles_r, tiles_c, tiles;  // tiles over the MMA rows (128) and columns (BN)
   int k_tiles, k_per_split, splits;
-  int units;    // tiles * splits
+  int units;    // tiles * splits (round-robin schedule)
+  int sk_grid;  // > 0: stream-K schedule over this many CTAs (= gridDim.x)
+  int64_t sk_work;  // stream-K: tiles * k_tiles K blocks in all
   int group_r;  // raster: groups of group_r row tiles, rows fastest inside a group
   int stream_b;  // 1: weights are read once (decode): L2 evict-first for them
   int pdl;       // 1: launched right behind our quantizer with programmatic dependent launch
@@ -128,11 +130,19 @@ struct GemmCfg {
   static constexpr int OUT_BYTES = SWAP ? BN * 64 : 2 * 32 * 64;
   static constexpr int SMEM_TILES = STAGES * STAGE_BYTES;
   static constexpr int SMEM_OUT = ((EPI_WARPS * OUT_BYTES + 1023) / 1024) * 1024;
-  static constexpr int NUM_BARS = 2 * STAGES + 2 * ACC_BUFS + 2;
+  static constexpr int NUM_BARS = 2 * STAGES + 2 * ACC_BUFS + 1 + ACT_KB;
+  static constexpr int ACT_RING = ACT_KB > 0 ? ACT_KB : 1;  // act_ready barriers (FUSE), at least 1 for the modulo
   static constexpr int SMEM_MISC = 16 + 4 * STAGES;  // TMEM slot, flags, last load per stage
   static constexpr int SMEM_BYTES =
       1024 + SMEM_TILES + SMEM_ACT + SMEM_OUT + SMEM_ACT_SCALES + NUM_BARS * 8 + SMEM_MISC;
   static_assert(SMEM_BYTES <= 232448, "more shared memory than one sm_100 CTA can have");
+  // Two producers and two MMA issuers take alternate K blocks.  With an even
+  // number of stages and of TMEM buffers, each stage and each buffer always
+  // belongs to the same producer and the same issuer, so a thread's wait on a
+  // barrier is never two phases ahead of it (a parity wait would then pass on
+  // the stale phase).  With an odd count, an issuer could reach stage s's
+  // next round while the other producer had not yet refilled it.
+  static_assert(STAGES % 2 == 0 && ACC_BUFS % 2 == 0, "stages and TMEM buffers must come in pairs");
   static_assert(TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM allocation");
   static_assert(STAGE_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "tiles must stay 1024-byte aligned");
 };
@@ -144,29 +154,70 @@ enum WaitSite : uint32_t {
   kWaitAccFull = 4,
   kWaitDrain = 5,
   kWaitMmaDone = 6,
-  kWaitActReady = 7,
+  kWaitActReady = 7,  // a resident activation K block (FUSE)
 };
 
+// A unit: one tile's K blocks kt0 .. kt1 - 1, the part `split` of the tile's
+// `pieces` parts (pieces > 1: partial sums meet in the workspace).
 struct UnitCoord {
-  int tile, tr, tc, kt0, kt1, split;
+  int tile, tr, tc, kt0, kt1, split, pieces;
 };
 
-// Unit u = split * tiles + tile.  Tiles are rasterised in groups of group_r
-// row tiles, row tiles fastest inside a group (the reference's order,
-// blockfp8 csrc/gemm_kernel.cuh:120-125); the host picks group_r so the
-// operand that is re-read stays in L2.
+// Two schedules of a CTA's units.
+// Round-robin split-K: unit u = split * tiles + tile, CTA b takes
+// u = b, b + gridDim.x, ... below p.units.
+// Stream-K (p.sk_grid > 0): the tiles' K blocks in one sequence (position
+// tile * k_tiles + kt), CTA b takes positions [W b / G, W (b + 1) / G) with
+// W = p.sk_work and G = p.sk_grid, so every CTA streams the same number of
+// K blocks (+-1); a unit is the part of one tile inside that range and u
+// is its first position.  The parts of a tile are numbered in K order.
+__device__ __forceinline__ int64_t sk_begin(const GemmParams& p, int b) {
+  return int64_t(b) * p.sk_work / p.sk_grid;
+}
+// Number of CTAs whose range starts at or before position x.
+__device__ __forceinline__ int sk_starts_upto(const GemmParams& p, int64_t x) {
+  const int64_t n = ((x + 1) * p.sk_grid + p.sk_work - 1) / p.sk_work;
+  return n < p.sk_grid ? int(n) : p.sk_grid;
+}
+__device__ __forceinline__ int first_unit(const GemmParams& p) {
+  return p.sk_grid > 0 ? int(sk_begin(p, blockIdx.x)) : int(blockIdx.x);
+}
+__device__ __forceinline__ bool unit_valid(const GemmParams& p, int u) {
+  return p.sk_grid > 0 ? u < sk_begin(p, blockIdx.x + 1) : u < p.units;
+}
+
+// Tiles are rasterised in groups of group_r row tiles, row tiles fastest
+// inside a group (the reference's order, blockfp8
+// csrc/gemm_kernel.cuh:120-125); the host picks group_r so the operand that
+// is re-read stays in L2.
 __device__ __forceinline__ UnitCoord unit_coord(const GemmParams& p, int u) {
   UnitCoord c;
-  c.tile = u % p.tiles;
-  c.split = u / p.tiles;
+  if (p.sk_grid > 0) {
+    c.tile = u / p.k_tiles;
+    c.kt0 = u % p.k_tiles;
+    const int64_t end = c.kt0 + (sk_begin(p, blockIdx.x + 1) - u);
+    c.kt1 = end < p.k_tiles ? int(end) : p.k_tiles;
+    const int64_t t0 = int64_t(c.tile) * p.k_tiles;
+    const int before = sk_starts_upto(p, t0);
+    c.split = sk_starts_upto(p, u) - before;
+    c.pieces = sk_starts_upto(p, t0 + p.k_tiles - 1) - before + 1;
+  } else {
+    c.tile = u % p.tiles;
+    c.split = u / p.tiles;
+    c.kt0 = c.split * p.k_per_split;
+    c.kt1 = min(p.k_tiles, c.kt0 + p.k_per_split);
+    c.pieces = p.splits;
+  }
   const int span = p.group_r * p.tiles_c;
   const int first = (c.tile / span) * p.group_r;
   const int rows = min(p.tiles_r - first, p.group_r);
   c.tr = first + (c.tile % span) % rows;
   c.tc = (c.tile % span) / rows;
-  c.kt0 = c.split * p.k_per_split;
-  c.kt1 = min(p.k_tiles, c.kt0 + p.k_per_split);
   return c;
+}
+
+__device__ __forceinline__ int next_unit(const GemmParams& p, int u, const UnitCoord& c) {
+  return p.sk_grid > 0 ? c.tile * p.k_tiles + c.kt1 : u + int(gridDim.x);
 }
 
 template <int N>
@@ -188,41 +239,67 @@ __device__ __forceinline__ uint32_t bf16x2_bits(float lo, float hi) {
 // In-kernel quantization of one unit's activations (FUSE): the tokens
 // tok0 .. tok0 + BN - 1 over K blocks kt0 .. kt1 - 1 become the unit's
 // resident B operand (one [BN x 128 B] 128-byte-swizzled tile per K block
-// at s_act + k * B_BYTES) and scales (s_act_scales[k * BN + token]).  The
-// epilogue's threads share the work: a half-warp per (K block, token) group,
-// QB groups per half-warp with all their loads issued first.  Real tokens
-// get the quantization kernel's arithmetic (amax from eps, IEEE amax / 448,
-// clamp, round-to-nearest-even e4m3 with saturation); tokens past M get zero
-// codes and a zero scale without dividing (a zero row divided by an
-// eps-sized scale would take the division's slow path for nothing).
+// at s_act + k * B_BYTES) and scales (s_act_scales[k * BN + token]).  Token
+// rows past M get zero codes and a zero scale with no load and no division.
+// The real (K block, token) groups go in K-block order to half-warps, QB
+// groups per half-warp per batch, the next batch's loads in flight while
+// this one is converted; after each batch the K blocks it completed are
+// released to the MMA issuers one by one, so the first MMAs start after the
+// first batch.  The K block at position q of the CTA's K-block sequence
+// (seq_base + k for the unit's block k) is released on act_ready[q % ACT_KB],
+// whose phase (q / ACT_KB) it completes: every position is released once, a
+// barrier serves positions ACT_KB apart -- the same MMA issuer (ACT_KB is
+// even), never two of one unit (no unit is longer) -- so an issuer's parity
+// wait is never a phase ahead of or behind the barrier.  Real tokens get the
+// quantization kernel's arithmetic: amax from eps, IEEE amax / 448, clamp,
+// round-to-nearest-even e4m3 with saturation.
 template <class Cfg>
 __device__ __forceinline__ void quantize_unit(const GemmParams& p, const UnitCoord& c, uint32_t s_act,
-                                              uint32_t s_act_scales, int ethread) {
-  constexpr int BN = Cfg::BN, QB = 4;
-  constexpr int HALVES = Cfg::EPI_THREADS / 16;
+                                              uint32_t s_act_scales, uint32_t act_ready0, int seq_base,
+                                              int ethread) {
+  constexpr int BN = Cfg::BN, QB = 8;
+  constexpr int ET = Cfg::EPI_THREADS, HALVES = ET / 16, STEP = HALVES * QB;
   const int lane16 = ethread & 15, half = ethread >> 4;
   const int tok0 = c.tc * BN;
   const int rows = min(BN, p.M - tok0);
-  const int groups = (c.kt1 - c.kt0) * BN;
-  // Every thread walks the same batches (the shuffle needs all 32 lanes);
-  // half-warp h takes groups g0 + h + b * HALVES of each batch.
-  for (int g0 = 0; g0 < groups; g0 += HALVES * QB) {
-    uint4 v[QB];
+  const int nkb = c.kt1 - c.kt0;
+  const int groups = nkb * rows;
+
+  // Padding token rows: zero codes (16 bytes per thread per step) and scales.
+  const int pad_units = nkb * (BN - rows) * 8;  // 16-byte units
+  for (int i = ethread; i < pad_units; i += ET) {
+    const int kl = i / ((BN - rows) * 8), rem = i % ((BN - rows) * 8);
+    const int row = rows + rem / 8, unit = rem % 8;
+    st_shared_v4(s_act + uint32_t(kl) * Cfg::B_BYTES + uint32_t(row) * 128u + uint32_t(unit) * 16u, 0u, 0u,
+                 0u, 0u);
+  }
+  for (int i = ethread; i < nkb * (BN - rows); i += ET) {
+    const int kl = i / (BN - rows), row = rows + i % (BN - rows);
+    st_shared_f32(s_act_scales + uint32_t(kl * BN + row) * 4u, 0.f);
+  }
+
+  auto load = [&](uint4 (&v)[QB], int g0) {
 #pragma unroll
     for (int b = 0; b < QB; ++b) {
-      const int g = g0 + half + b * HALVES;
-      const int kl = g / BN, row = g % BN;
+      const int gi = g0 + half + b * HALVES;
+      const int kl = gi / rows, row = gi % rows;
       const int col = (c.kt0 + kl) * 128 + lane16 * 8;
-      v[b] = make_uint4(0u, 0u, 0u, 0u);
-      if (g < groups && row < rows && col < p.K)
+      v[b] = make_uint4(0u, 0u, 0u, 0u);  // past K: zeros, which leave the amax alone
+      if (gi < groups && col < p.K)
         v[b] = __ldg(reinterpret_cast<const uint4*>(p.x + int64_t(tok0 + row) * p.ldx + col));
     }
+  };
+  uint4 cur[QB], nxt[QB];
+  load(cur, 0);
+  int released = 0;  // K blocks of this unit already handed to the MMA issuers
+  // Every thread walks the same batches (the shuffle needs all 32 lanes).
+  for (int g0 = 0; g0 < groups; g0 += STEP) {
+    if (g0 + STEP < groups) load(nxt, g0 + STEP);
 #pragma unroll
     for (int b = 0; b < QB; ++b) {
-      const int g = g0 + half + b * HALVES;
-      const int kl = g / BN, row = g % BN;
-      const bool real = g < groups && row < rows;
-      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v[b]);
+      const int gi = g0 + half + b * HALVES;
+      const int kl = gi / rows, row = gi % rows;
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&cur[b]);
       float f[8];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -235,11 +312,9 @@ __device__ __forceinline__ void quantize_unit(const GemmParams& p, const UnitCoo
       for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(f[e]));
 #pragma unroll
       for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-      if (g >= groups) continue;
-      uint32_t packed[2] = {0u, 0u};
-      float scale = 0.f;
-      if (real) {
-        scale = amax / 448.f;
+      if (gi < groups) {
+        const float scale = amax / 448.f;
+        uint32_t packed[2] = {0u, 0u};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float2 q = make_float2(fminf(fmaxf(f[2 * e] / scale, -448.f), 448.f),
@@ -247,17 +322,25 @@ __device__ __forceinline__ void quantize_unit(const GemmParams& p, const UnitCoo
           const uint32_t pair = __nv_cvt_float2_to_fp8x2(q, __NV_SATFINITE, __NV_E4M3);
           packed[e >> 1] |= pair << (16 * (e & 1));
         }
+        // 8 codes of chunk lane16 of token row `row`: 16-byte unit lane16 / 2
+        // of the row, XOR-swizzled with the row inside its 8-row group.
+        const uint32_t unit16 = uint32_t(lane16 >> 1) ^ uint32_t(row & 7);
+        st_shared_v2(s_act + uint32_t(kl) * Cfg::B_BYTES + uint32_t(row) * 128u + unit16 * 16u +
+                         uint32_t(lane16 & 1) * 8u,
+                     packed[0], packed[1]);
+        if (lane16 == 0) st_shared_f32(s_act_scales + uint32_t(kl * BN + row) * 4u, scale);
       }
-      // 8 codes of chunk lane16 of token row `row`: 16-byte unit lane16 / 2
-      // of the row, XOR-swizzled with the row inside its 8-row group.
-      const uint32_t unit16 = uint32_t(lane16 >> 1) ^ uint32_t(row & 7);
-      st_shared_v2(s_act + uint32_t(kl) * Cfg::B_BYTES + uint32_t(row) * 128u + unit16 * 16u +
-                       uint32_t(lane16 & 1) * 8u,
-                   packed[0], packed[1]);
-      if (lane16 == 0) st_shared_f32(s_act_scales + uint32_t(kl * BN + row) * 4u, scale);
     }
+    fence_proxy_async_smem();  // the MMAs read the operand through the async proxy
+    named_bar_sync(1, ET);
+    const int done = min(nkb, min(groups, g0 + STEP) / rows);  // whole K blocks finished
+    if (ethread == 0)
+      for (; released < done; ++released)
+        mbar_arrive(act_ready0 + 8u * uint32_t((seq_base + released) % Cfg::ACT_RING));
+    released = done;
+#pragma unroll
+    for (int b = 0; b < QB; ++b) cur[b] = nxt[b];
   }
-  fence_proxy_async_smem();  // the MMAs read the operand through the async proxy
 }
 
 template <class Cfg>
@@ -280,7 +363,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
   auto acc_full = [&](int a) { return s_bars + 8u * (2 * STAGES + a); };
   auto acc_empty = [&](int a) { return s_bars + 8u * (2 * STAGES + ACC_BUFS + a); };
   const uint32_t mma_done = s_bars + 8u * (2 * STAGES + 2 * ACC_BUFS);
-  const uint32_t act_ready = s_bars + 8u * (2 * STAGES + 2 * ACC_BUFS + 1);
+  const uint32_t act_ready0 = s_bars + 8u * (2 * STAGES + 2 * ACC_BUFS + 1);  // FUSE: [ACT_KB], by position
   uint32_t* misc = reinterpret_cast<uint32_t*>(smem + (s_bars - base) + 8 * Cfg::NUM_BARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 1);
   volatile int* last_flag = reinterpret_cast<volatile int*>(misc + 2);
@@ -297,8 +380,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
       mbar_init(acc_full(a), 1);
       mbar_init(acc_empty(a), Cfg::EPI_WARPS);
     }
-    mbar_init(mma_done, 2);   // one commit from each MMA issuer
-    mbar_init(act_ready, 1);  // FUSE: a unit's quantized activations are in place
+    mbar_init(mma_done, 2);  // one commit from each MMA issuer
+    for (int k = 0; k < Cfg::ACT_KB; ++k) mbar_init(act_ready0 + 8u * k, 1);  // FUSE: activations in place
     *abort_flag = 0;
     for (int st = 0; st < STAGES; ++st) stage_seq[st] = -1;
     fence_barrier_init();
@@ -350,8 +433,9 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
         int early = 0;  // K blocks (of the whole sequence) whose weights went out early
         if (p.pdl && !FUSE) {
           int seq = 0;
-          for (int u = blockIdx.x; u < p.units && seq < STAGES; u += gridDim.x) {
+          for (int u = first_unit(p); unit_valid(p, u) && seq < STAGES;) {
             const UnitCoord c = unit_coord(p, u);
+            u = next_unit(p, u, c);
             for (int kt = c.kt0; kt < c.kt1 && seq < STAGES; ++kt, ++seq) {
               if ((seq & 1) != role) continue;
               const uint32_t dst = s_tiles + uint32_t(seq) * Cfg::STAGE_BYTES;  // stage = seq
@@ -365,8 +449,9 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
         if (!FUSE) griddep_wait();  // activations are the previous kernel's output
         int seq = 0;
         bool ok = true;
-        for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
+        for (int u = first_unit(p); ok && unit_valid(p, u);) {
           const UnitCoord c = unit_coord(p, u);
+          u = next_unit(p, u, c);
           for (int kt = c.kt0; kt < c.kt1; ++kt, ++seq) {
             if ((seq & 1) != role) continue;
             const int stage = seq % STAGES;
@@ -394,13 +479,18 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
         // which never carries out (shared memory ends below 256 KB).
         const uint64_t desc_a0 = smem_desc_k128_sw128(s_tiles);
         const uint64_t desc_b0 = smem_desc_k128_sw128(FUSE ? s_act : s_tiles + Cfg::A_BYTES);
-        int seq = 0, unit_no = 0;
+        int seq = 0;
         bool ok = true;
-        for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x, ++unit_no) {
+        for (int u = first_unit(p); ok && unit_valid(p, u);) {
           const UnitCoord c = unit_coord(p, u);
-          if (FUSE && !mbar_wait(act_ready, uint32_t(unit_no) & 1u, abort_flag, kWaitActReady)) break;
+          u = next_unit(p, u, c);
           for (int kt = c.kt0; kt < c.kt1; ++kt, ++seq) {
             if ((seq & 1) != role) continue;
+            if (FUSE && !mbar_wait(act_ready0 + 8u * uint32_t(seq % Cfg::ACT_RING),
+                                   uint32_t(seq / Cfg::ACT_RING) & 1u, abort_flag, kWaitActReady)) {
+              ok = false;
+              break;
+            }
             const int stage = seq % STAGES, acc = seq % ACC_BUFS;
             const uint32_t phase = uint32_t(seq / STAGES) & 1u;
             const uint32_t acc_phase = uint32_t(seq / ACC_BUFS) & 1u;
@@ -484,38 +574,50 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
       }
       return q;
     };
-    // Scales of the next PF K blocks, in flight ahead of their use.
-    float pa[PF], pa2[PF], pb[PF];
-    auto load_scales = [&](const ScaleSrc& q, int kt, int j) {
-      pa[j] = q.sa_ok ? __ldg(q.sa + int64_t(kt) * p.sa_k) : 0.f;
-      if constexpr (SWAP && BN > 32) pa2[j] = q.sa2_ok ? __ldg(q.sa2 + int64_t(kt) * p.sa_k) : 0.f;
-      pb[j] = q.sb_ok ? __ldg(q.sb + int64_t(kt) * p.sb_k) : 0.f;
+    // Scales of a unit's K blocks kt0 + j, j < PF, ride in pa/pa2/pb[j] and
+    // are refilled PF K blocks ahead of their use; the next unit's first PF
+    // scales go out into na/na2/nb when the current unit starts, so they are
+    // in place at the unit boundary (a load issued while the weights stream
+    // at full speed can take microseconds).
+    float pa[PF], pa2[PF], pb[PF], na[PF], na2[PF], nb[PF];
+    auto load_scales = [&](const ScaleSrc& q, int kt, float& a, float& a2, float& b) {
+      a = q.sa_ok ? ldg_pinned(q.sa + int64_t(kt) * p.sa_k) : 0.f;
+      if constexpr (SWAP && BN > 32) a2 = q.sa2_ok ? ldg_pinned(q.sa2 + int64_t(kt) * p.sa_k) : 0.f;
+      b = q.sb_ok ? ldg_pinned(q.sb + int64_t(kt) * p.sb_k) : 0.f;
     };
-    auto prefetch_unit = [&](const ScaleSrc& q, const UnitCoord& c) {
+    auto prefetch_unit = [&](const UnitCoord& c, float (&a)[PF], float (&a2)[PF], float (&b)[PF]) {
+      const ScaleSrc q = scale_src(c);
 #pragma unroll
       for (int j = 0; j < PF; ++j)
-        if (c.kt0 + j < c.kt1) load_scales(q, c.kt0 + j, j);
+        if (c.kt0 + j < c.kt1) load_scales(q, c.kt0 + j, a[j], a2[j], b[j]);
     };
-    // FUSE: quantize a unit's activations, then hand them to the MMA issuers.
-    auto publish_unit = [&](const UnitCoord& c) {
-      if constexpr (FUSE) {
-        quantize_unit<Cfg>(p, c, s_act, s_act_scales, ew * 32 + lane);
-        named_bar_sync(1, Cfg::EPI_THREADS);
-        if (ew == 0 && lane == 0) mbar_arrive(act_ready);
-      }
+    // FUSE: quantize a unit's activations, handing each K block to the MMA
+    // issuers as soon as it is in place; seq_base = the unit's first position
+    // in the CTA's K-block sequence.
+    auto publish_unit = [&](const UnitCoord& c, int seq_base) {
+      if constexpr (FUSE) quantize_unit<Cfg>(p, c, s_act, s_act_scales, act_ready0, seq_base, ew * 32 + lane);
     };
 
     if (!FUSE) griddep_wait();  // activation scales are the previous kernel's output
-    UnitCoord c_next = unit_coord(p, blockIdx.x < p.units ? blockIdx.x : 0);
-    ScaleSrc src_next = scale_src(c_next);
-    if (blockIdx.x < p.units) {
-      prefetch_unit(src_next, c_next);
-      publish_unit(c_next);
+    const int u0 = first_unit(p);
+    const bool any_unit = unit_valid(p, u0);
+    UnitCoord c_next = unit_coord(p, any_unit ? u0 : 0);
+    if (any_unit) {
+      prefetch_unit(c_next, pa, pa2, pb);
+      publish_unit(c_next, 0);
     }
 
-    for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
+    int next_seq = 0;  // position of the next unit's first K block in the CTA's sequence
+    for (int u = u0; any_unit && unit_valid(p, u);) {
       const UnitCoord c = c_next;
-      const ScaleSrc src = src_next;
+      u = next_unit(p, u, c);
+      next_seq += c.kt1 - c.kt0;
+      const ScaleSrc src = scale_src(c);
+      const bool more = unit_valid(p, u);
+      if (more) {
+        c_next = unit_coord(p, u);
+        prefetch_unit(c_next, na, na2, nb);
+      }
       const int r = c.tr * 128 + row;                       // this thread's MMA row
       const bool row_ok = r < rows_total;
       const bool warp_rows = c.tr * 128 + 32 * quarter < rows_total;  // warp-uniform
@@ -536,7 +638,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
             float sa_v = pa[j], sb_v = pb[j];
             float sa2_v = 0.f;
             if constexpr (SWAP && BN > 32) sa2_v = pa2[j];
-            if (kt + PF < c.kt1) load_scales(src, kt + PF, j);
+            if (kt + PF < c.kt1) load_scales(src, kt + PF, pa[j], pa2[j], pb[j]);
             if constexpr (FUSE) {  // the token scales quantize_unit wrote for this K block
               const uint32_t sl = s_act_scales + uint32_t((kt - c.kt0) * BN) * 4u;
               sa_v = lane < BN ? ld_shared_f32(sl + uint32_t(lane) * 4u) : 0.f;
@@ -582,22 +684,25 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
         }
       }
 
-      // The next unit's first scales go out now, ahead of this unit's
-      // split-K hand-off and store; FUSE also quantizes the next unit here
-      // (all of this unit's MMAs are done: every K block's partial has been
-      // read, and every epilogue thread is past its scales).
-      if (u + int(gridDim.x) < p.units) {
-        c_next = unit_coord(p, u + gridDim.x);
-        src_next = scale_src(c_next);
-        prefetch_unit(src_next, c_next);
+      // The next unit's scales move into the ring; FUSE quantizes the next
+      // unit now, ahead of this unit's split-K hand-off and store (all of
+      // this unit's MMAs are done: every K block's partial has been read,
+      // and every epilogue thread is past its scales).
+      if (more) {
+#pragma unroll
+        for (int j = 0; j < PF; ++j) {
+          pa[j] = na[j];
+          pa2[j] = na2[j];
+          pb[j] = nb[j];
+        }
         if constexpr (FUSE) {
           named_bar_sync(1, Cfg::EPI_THREADS);
-          publish_unit(c_next);
+          publish_unit(c_next, next_seq);
         }
       }
 
       bool store = work;
-      if (p.splits > 1) {
+      if (c.pieces > 1) {
         // Deterministic split-K: publish this split's partial, count arrivals;
         // the last CTA of the tile sums all partials in split order.
         const int64_t split_stride = int64_t(p.tiles) * (128 * BN);
@@ -615,15 +720,12 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
             for (int j = 0; j < COLS; ++j) __stcg(w + j * 128, accum[j]);
           }
         }
-        // Release: every epilogue thread's partial is ordered before the
-        // counter update by the barrier and lane 0's gpu-scope fence.
+        // Every epilogue thread's partial is ordered before the counter
+        // update by the barrier and lane 0's gpu-scope release; its acquire
+        // makes the other parts' partials visible to the last arriver.
         named_bar_sync(1, Cfg::EPI_THREADS);
-        if (ew == 0 && lane == 0) {
-          fence_acq_rel_gpu();
-          const bool is_last = atomicAdd(p.counters + c.tile, 1) == p.splits - 1;
-          if (is_last) fence_acq_rel_gpu();  // acquire: the other splits' partials
-          *last_flag = is_last;
-        }
+        if (ew == 0 && lane == 0)
+          *last_flag = atom_add_acq_rel_gpu(p.counters + c.tile, 1) == c.pieces - 1;
         named_bar_sync(1, Cfg::EPI_THREADS);
         const bool last = *last_flag != 0;
         store = store && last;
@@ -634,7 +736,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
             // one pass per split with all of a split's loads in flight.
 #pragma unroll
             for (int j = 0; j < COLS; ++j) accum[j] = 0.f;
-            for (int s = 0; s < p.splits; ++s) {
+            for (int s = 0; s < c.pieces; ++s) {
               if constexpr (!SWAP) {
                 const float* w = ws_tile + s * split_stride + row * BN + g * COLS;
 #pragma unroll

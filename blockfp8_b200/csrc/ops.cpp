@@ -88,9 +88,10 @@ void run(const bfp8_gemm_problem& p, bfp8_plan plan, int64_t config, int64_t spl
   if (config >= 0) {
     TORCH_CHECK(config < num_configs, "blockfp8: config out of range");
     plan.config = int(config);
-    if (split_k <= 0) split_k = 1;
+    if (split_k == 0) split_k = 1;
   }
-  if (split_k > 0) plan.splits = int(split_k);
+  // split_k > 0: that many K splits; < 0: stream-K over -split_k CTAs; 0: the plan's
+  if (split_k != 0) plan.splits = int(split_k);
 
   at::Tensor workspace;
   float* ws = nullptr;

@@ -197,6 +197,19 @@ __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wa
 
 // gpu-scope acquire-release fence (split-K counter hand-off).
 __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+// A read-only global load the compiler keeps where it is written (a prefetch
+// must go out early, not next to its use).
+__device__ __forceinline__ float ldg_pinned(const float* ptr) {
+  float v;
+  asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v) : "l"(ptr));
+  return v;
+}
+// Atomic add with acquire-release semantics at GPU scope; returns the old value.
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* ptr, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(ptr), "r"(v) : "memory");
+  return old;
+}
 
 // ---- named barriers (a subset of the CTA's warps) ---------------------------------
 

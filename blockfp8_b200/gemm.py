@@ -84,7 +84,8 @@ def gemm(
 ) -> torch.Tensor:
     """C [M, N] bf16 = block-scaled A_q [M, K] @ B_q [N, K]^T (layouts in
     blockfp8_b200.layout).  config / split_k override the planner's choice
-    (-1 / 0 = automatic); configs() lists the compiled configurations."""
+    (-1 / 0 = automatic; split_k < 0 = stream-K over -split_k CTAs);
+    configs() lists the compiled configurations."""
     m, n, _ = check_gemm_args(a_q, a_scales, b_q, b_scales, out_dtype)
     if not a_q.is_cuda:
         raise ValueError("gemm runs on CUDA tensors only; use blockfp8.reference_gemm on CPU")

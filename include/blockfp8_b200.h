@@ -54,9 +54,20 @@ typedef struct bfp8_gemm_problem {
 /* Kernel choice; replaces blockfp8::Plan (csrc/blockfp8.h:32-36). */
 typedef struct bfp8_plan {
   int config; /* index into the compiled (fused, if fused) configurations */
-  int splits; /* K splits (1 = no split-K) */
-  int fused;  /* nonzero: A is bf16 and is quantized as part of the call */
+  int splits; /* K splits (1 = no split-K); negative: stream-K, -splits CTAs
+                 share all tiles' K blocks evenly, each tile's parts summed
+                 in K order (deterministic) */
+  int fused;  /* 0: A is e4m3 with scales sa; nonzero: A is bf16 and is
+                 quantized as part of the call, by a quantization kernel
+                 into the workspace ahead of the GEMM (BFP8_FUSED_QUANT_KERNEL)
+                 or, for BFP8_FUSED_IN_GEMM, inside the GEMM kernel itself
+                 where the configuration has that variant and one split's K
+                 range fits its resident operand (else as QUANT_KERNEL).
+                 Results are bit-identical either way. */
 } bfp8_plan;
+
+#define BFP8_FUSED_QUANT_KERNEL 1
+#define BFP8_FUSED_IN_GEMM 2
 
 /* Activation quantization problem; replaces blockfp8::QuantProblem
  * (csrc/blockfp8.h:66-75): x [M, K] bf16 (row stride ldx) -> q [M, K] e4m3
@@ -84,6 +95,8 @@ const char* bfp8_fused_config_name(int config);
  * (csrc/blockfp8.h:43-45).  num_sms = the device's multiprocessor count. */
 bfp8_plan bfp8_choose_plan(int M, int N, int K, int num_sms);
 bfp8_plan bfp8_choose_fused_plan(int M, int N, int K, int num_sms);
+/* (choose_fused_plan's plan.fused is the faster of the two fused modes for
+ * the shape, as tuned on a B200.) */
 
 /* Whether linear runs this shape through the fused path; replaces
  * prefers_fused (csrc/blockfp8.h:47-50).  Returns 0 or 1. */

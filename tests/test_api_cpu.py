@@ -145,7 +145,7 @@ def test_c_abi_answers_without_a_gpu():
         plan = lib.bfp8_choose_plan(m, nn, k, 148)
         assert 0 <= plan.config < n and plan.splits >= 1 and plan.fused == 0
         fplan = lib.bfp8_choose_fused_plan(m, nn, k, 148)
-        assert fplan.fused == 1
+        assert fplan.fused in (1, 2)
         p = _native.GemmProblem(M=m, N=nn, K=k)
         tiles, kt = ctypes.c_int(), ctypes.c_int()
         assert lib.bfp8_plan_shape(ctypes.byref(p), plan, ctypes.byref(tiles), ctypes.byref(kt)) == 0
@@ -154,15 +154,66 @@ def test_c_abi_answers_without_a_gpu():
         cnt = lib.bfp8_counters_needed(ctypes.byref(p), plan)
         splits = -(-kt.value // -(-kt.value // min(plan.splits, kt.value)))
         assert (ws == 0) == (splits == 1) and (cnt == 0) == (splits == 1)
-        fws = lib.bfp8_workspace_bytes(ctypes.byref(p), fplan)
-        if names[fplan.config].startswith("m"):  # quantization kernel first: q and s live there
-            assert fws >= m * k
-        else:  # swapped tiles quantize inside the GEMM: only split-K scratch
-            assert fws == lib.bfp8_workspace_bytes(ctypes.byref(p), plan)
+        # quantization kernel first: q and s live in the front of the workspace
+        q_plan = _native.Plan(plan.config, plan.splits, 1)
+        assert lib.bfp8_workspace_bytes(ctypes.byref(p), q_plan) >= m * k + ws
+        # quantization inside the GEMM: only split-K scratch where the
+        # configuration has that variant and a split's K blocks fit its
+        # resident operand (64 KB of BN x 128 e4m3 tiles), else as above
+        for config in range(n):
+            for splits in (1, 2, 4, 8):
+                in_plan, q_plan = _native.Plan(config, splits, 2), _native.Plan(config, splits, 1)
+                p_plan = _native.Plan(config, splits, 0)
+                bn = int(re.match(r"[mw]128[nt](\d+)", names[config]).group(1))
+                per = -(-kt.value // min(splits, kt.value))
+                fits = names[config].startswith("w") and per * bn * 128 <= 65536
+                expect = p_plan if fits else q_plan
+                assert lib.bfp8_workspace_bytes(ctypes.byref(p), in_plan) == \
+                    lib.bfp8_workspace_bytes(ctypes.byref(p), expect)
     bad = _native.Plan(99, 1, 0)
     p = _native.GemmProblem(M=1, N=128, K=128)
     assert lib.bfp8_workspace_bytes(ctypes.byref(p), bad) < 0
     assert "config" in lib.bfp8_last_error().decode()
+
+
+def _stream_k_parts(tiles, k_tiles, ctas):
+    """Parts per tile when ctas CTAs take the K-block positions
+    [W b / G, W (b + 1) / G) of the tiles' K blocks in sequence."""
+    work = tiles * k_tiles
+    g = max(1, min(ctas, work))
+    starts = [b * work // g for b in range(g)]
+    parts = [1] * tiles
+    for s_ in starts:
+        if s_ % k_tiles:
+            parts[s_ // k_tiles] += 1
+    return parts, min(k_tiles, -(-work // g))  # a unit never leaves its tile
+
+
+@pytest.mark.parametrize("m, n, k, ctas", [(1, 24576, 4096, 148), (16, 4096, 12288, 148),
+                                           (37, 392, 2064, 5), (37, 392, 2064, 1000), (1, 128, 128, 148),
+                                           (8192, 24576, 4096, 148)])
+def test_stream_k_plan_sizes(m, n, k, ctas):
+    """Workspace and counters of a stream-K plan (splits = -CTAs): the most
+    parts any tile is cut into, times the tiles' fp32 partial tiles."""
+    lib = _native.capi()
+    names = [lib.bfp8_config_name(i).decode() for i in range(lib.bfp8_num_configs())]
+    p = _native.GemmProblem(M=m, N=n, K=k)
+    for config, name in enumerate(names):
+        bn = int(re.match(r"[mw]128[nt](\d+)", name).group(1))
+        rows, cols = (n, m) if name.startswith("w") else (m, n)
+        tiles = -(-rows // 128) * -(-cols // bn)
+        parts, longest = _stream_k_parts(tiles, -(-k // 128), ctas)
+        plan = _native.Plan(config, -ctas, 0)
+        most = max(parts)
+        expect_ws = 0 if most == 1 else most * tiles * 128 * bn * 4
+        assert lib.bfp8_workspace_bytes(ctypes.byref(p), plan) == expect_ws
+        assert lib.bfp8_counters_needed(ctypes.byref(p), plan) == (0 if most == 1 else tiles)
+        # in-GEMM quantization needs the longest unit to fit the resident operand
+        fits = name.startswith("w") and longest * bn * 128 <= 65536
+        in_plan = _native.Plan(config, -ctas, 2)
+        front = lib.bfp8_workspace_bytes(ctypes.byref(p), _native.Plan(config, -ctas, 1)) - expect_ws
+        assert front > 0
+        assert lib.bfp8_workspace_bytes(ctypes.byref(p), in_plan) == expect_ws + (0 if fits else front)
 
 
 def test_c_abi_rejects_bad_problems_without_launching():
@@ -170,6 +221,9 @@ def test_c_abi_rejects_bad_problems_without_launching():
     p = _native.GemmProblem(M=4, N=256, K=200)  # K % 16 != 0
     assert lib.bfp8_launch_gemm(ctypes.byref(p), _native.Plan(0, 1, 0), None, None, None) == -1
     assert "K must be" in lib.bfp8_last_error().decode()
+    p = _native.GemmProblem(M=4, N=256, K=256)
+    assert lib.bfp8_launch_gemm(ctypes.byref(p), _native.Plan(0, 0, 0), None, None, None) == -1
+    assert "splits" in lib.bfp8_last_error().decode()
     q = _native.QuantProblem(M=4, K=12)
     assert lib.bfp8_launch_quantize(ctypes.byref(q), None) == -1
 

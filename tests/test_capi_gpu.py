@@ -100,3 +100,37 @@ def test_bad_arguments_come_back_as_errors():
     plan.config = 99
     with pytest.raises(RuntimeError, match="config"):
         capi.launch_gemm(p, plan)
+
+
+# ---- the two fused modes --------------------------------------------------------
+
+IN_GEMM_CASES = [
+    (1, 24576, 2048 + 128, 3),   # 192 tiles x 3 ragged splits: several units per CTA, short last split
+    (5, 4096, 4096, 1),          # one split of 32 K blocks: fits only the 16-token tiles
+    (17, 6144, 4096 + 16, 4),    # ragged K tail, tokens past one tile
+    (33, 2048, 12288, 12),       # down-like K
+    (64, 1024, 4096, 8),
+    (1, 24576, 4096, -148),      # stream-K: 41-42 K blocks per CTA across tile boundaries
+    (16, 4096, 12288, -148),
+    (7, 6144, 4096, -37),
+]
+
+
+@pytest.mark.parametrize("m, n, k, splits", IN_GEMM_CASES)
+def test_both_fused_modes_equal_the_quantized_gemm(m, n, k, splits):
+    """Quantization inside the GEMM (fused mode 2) and the quantization kernel
+    + GEMM (mode 1) give the pre-quantized GEMM's bits under every
+    configuration; mode 2 falls back to mode 1 where the plan's K range does
+    not fit the resident operand or the configuration has no such variant."""
+    b_np, sb_np, b, sb = _weights(n, k, seed=3)
+    x = bf16_activations(m, k, seed=7 + m, ties=True).to(DEV)
+    q, s = capi.quantize(x)
+    lib = _native.capi()
+    for config in range(lib.bfp8_num_configs()):
+        expect = capi.gemm(q, s, b, sb, config=config, splits=splits)
+        for mode in (1, 2):
+            got = capi.gemm(x, None, b, sb, config=config, splits=splits, fused=mode)
+            assert torch.equal(got, expect), (config, mode)
+    a_np, sa_np = oracle_quant(x.cpu())
+    assert_close(expect, O.reference_gemm(a_np, sa_np, b_np, sb_np))
+    assert _native.device_status(reset=True) == 0

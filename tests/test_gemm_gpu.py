@@ -65,6 +65,38 @@ def test_exact_integer_case_split_k(config, splits):
     assert_exact(c, oracle_gemm(a, sa, b, sb))
 
 
+@pytest.mark.parametrize("config", CONFIGS)
+@pytest.mark.parametrize("shape, ctas", [((37, 392, 2048 + 16), 148), ((37, 392, 2048 + 16), 5),
+                                         ((37, 392, 2048 + 16), 1000), ((1, 24576, 4096), 148),
+                                         ((20, 4096, 12288), 148), ((3, 1000, 1040), 7)])
+def test_exact_integer_case_stream_k(config, shape, ctas):
+    """Stream-K (split_k < 0): CTAs share all tiles' K blocks evenly; tiles cut
+    into several parts (ragged, across tile boundaries) sum them in K order."""
+    a, sa, b, sb = integer_operands(*shape, seed=ctas % 97)
+    c = blockfp8.gemm(a, sa, b, sb, config=config, split_k=-ctas)
+    assert_exact(c, oracle_gemm(a, sa, b, sb))
+
+
+@pytest.mark.parametrize("config", CONFIGS)
+def test_stream_k_deterministic_and_in_graph(config):
+    a, sa, b, sb = realistic_operands(9, 6144, 4096, seed=8)
+    outs = [blockfp8.gemm(a, sa, b, sb, config=config, split_k=-148) for _ in range(3)]
+    assert all(torch.equal(outs[0], o) for o in outs[1:])
+    assert_close(outs[0], oracle_gemm(a, sa, b, sb))
+    graph = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        blockfp8.gemm(a, sa, b, sb, config=config, split_k=-148)
+        with torch.cuda.graph(graph, stream=s):
+            out = blockfp8.gemm(a, sa, b, sb, config=config, split_k=-148)
+    torch.cuda.current_stream().wait_stream(s)
+    for _ in range(3):  # the counters are back at zero after every replay
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, outs[0])
+
+
 @pytest.mark.parametrize("shape", SHAPES + [(1, 4096, 4096), (64, 6144, 4096), (512, 4096, 12288),
                                             (384, 4096, 12288), (768, 6144, 4096)])
 def test_realistic_within_tolerance_auto_plan(shape):
