@@ -40,16 +40,18 @@ def candidates(m, n, k, num_configs, names, num_sms=148):
         swap = names[config].startswith("w")
         if swap and m > 64:
             continue
+        bm = int(names[config][1:].split("t" if swap else "n")[0])
         bn = int(names[config].split("t" if swap else "n")[1].split("s")[0])
-        tiles = (-(-(n if swap else m) // 128)) * (-(-(m if swap else n) // bn))
+        tiles = (-(-(n if swap else m) // bm)) * (-(-(m if swap else n) // bn))
+        slots = num_sms // (bm // 128)  # a 256-row tile takes a CTA pair
         for splits in SPLITS:
-            if splits > kt or (splits > 1 and tiles >= 2 * num_sms):
+            if splits > kt or (splits > 1 and tiles >= 2 * slots):
                 continue
             per = -(-kt // splits)
             if -(-kt // per) != splits:
                 continue
             yield config, splits
-        if tiles < 4 * num_sms and tiles % num_sms and tiles * kt >= 2 * num_sms:
+        if bm == 128 and tiles < 4 * num_sms and tiles % num_sms and tiles * kt >= 2 * num_sms:
             yield config, -num_sms  # stream-K: every SM the same number of K blocks
 
 

@@ -46,6 +46,8 @@ struct ConfigEntry {
   const char* name;
   int bn, stages, threads, smem;
   bool swap;  // MMA rows are weight rows, columns are tokens (decode)
+  int bm;     // MMA rows of a tile: 128, or 256 for a CTA pair
+  bool pair;  // a cluster of two CTAs per tile (cta_group::2)
   const void* kernel;
   void (*launch)(const GemmParams&, int grid, cudaStream_t);
   // Swapped configurations also come with the activation quantization done
@@ -63,17 +65,26 @@ void launch_cfg(const GemmParams& gp, int grid, cudaStream_t stream) {
   cfg.blockDim = dim3(Cfg::THREADS);
   cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (gp.pdl) {  // only right behind our own quantizer
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n++].val.programmaticStreamSerializationAllowed = 1;
+  }
+  if (Cfg::PAIR) {  // CTA pairs: clusters of two along x
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = 2;
+    attr[n].val.clusterDim.y = 1;
+    attr[n++].val.clusterDim.z = 1;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = gp.pdl ? 1 : 0;  // only right behind our own quantizer
+  cfg.numAttrs = n;
   cudaLaunchKernelEx(&cfg, gemm_kernel<Cfg>, gp);
 }
 
 template <class Cfg>
 ConfigEntry entry(const char* name) {
-  return {name, Cfg::BN, Cfg::STAGES, Cfg::THREADS, Cfg::SMEM_BYTES, Cfg::SWAP,
+  return {name, Cfg::BN, Cfg::STAGES, Cfg::THREADS, Cfg::SMEM_BYTES, Cfg::SWAP, Cfg::TILE_M, Cfg::PAIR,
           reinterpret_cast<const void*>(&gemm_kernel<Cfg>), &launch_cfg<Cfg>};
 }
 
@@ -88,7 +99,8 @@ ConfigEntry entry_fused(const char* name) {
   return e;
 }
 
-// Normal order: "m128n<BN>": 128 activation rows x BN weight rows per tile.
+// Normal order: "m128n<BN>": 128 activation rows x BN weight rows per tile;
+// "m256n256": 256 x 256 tiles on a CTA pair (cta_group::2, prefill).
 // Swapped order: "w128t<BN>": 128 weight rows x BN tokens per tile (decode).
 //                        BN  stages  swapped
 using Cfg256 = GemmCfg<256, 4, false>;
@@ -102,6 +114,8 @@ using CfgW64 = GemmCfg<64, 8, true>;
 using CfgW16Q = GemmCfg<16, 8, true, true>;
 using CfgW32Q = GemmCfg<32, 8, true, true>;
 using CfgW64Q = GemmCfg<64, 8, true, true>;
+// ... a CTA pair: 32 KB per CTA per stage (its 128 A rows, half the B rows)
+using CfgP256 = GemmCfg<256, 6, false, false, true>;
 
 const ConfigEntry kConfigs[] = {
     entry<Cfg256>("m128n256s4"),
@@ -110,6 +124,7 @@ const ConfigEntry kConfigs[] = {
     entry_fused<CfgW16, CfgW16Q>("w128t16s10"),
     entry_fused<CfgW32, CfgW32Q>("w128t32s10"),
     entry_fused<CfgW64, CfgW64Q>("w128t64s8"),
+    entry<CfgP256>("m256n256s6"),
 };
 constexpr int kNumConfigs = int(sizeof(kConfigs) / sizeof(kConfigs[0]));
 // The fused path (gemm_bf16) quantizes into the workspace, then runs the
@@ -258,11 +273,14 @@ double plan_cost_ns(int M, int N, int K, int num_sms, int config, int splits) {
   const ConfigEntry& e = kConfigs[config];
   const int k_tiles = cdiv(K, 128);
   const int rows_total = e.swap ? N : M, cols_total = e.swap ? M : N;
-  const int tiles_r = cdiv(rows_total, 128), tiles_c = cdiv(cols_total, e.bn);
+  const int tiles_r = cdiv(rows_total, e.bm), tiles_c = cdiv(cols_total, e.bn);
+  const int ctas_per_unit = e.pair ? 2 : 1;
+  const int slots = std::max(1, num_sms / ctas_per_unit);  // units in flight at once
   int per, real_splits;
   int64_t waves;
   int active;
   if (splits < 0) {
+    if (e.pair) return 1e300;  // no stream-K schedule for CTA pairs
     const int64_t work = int64_t(tiles_r) * tiles_c * k_tiles;
     const int64_t g = std::max<int64_t>(1, std::min<int64_t>(-int64_t(splits), work));
     per = int((work + g - 1) / g);
@@ -274,13 +292,14 @@ double plan_cost_ns(int M, int N, int K, int num_sms, int config, int splits) {
     per = cdiv(k_tiles, std::max(1, std::min(splits, k_tiles)));
     real_splits = cdiv(k_tiles, per);
     const int64_t units = int64_t(tiles_r) * tiles_c * real_splits;
-    waves = (units + num_sms - 1) / num_sms;
-    active = int(std::min<int64_t>(units, num_sms));
+    waves = (units + slots - 1) / slots;
+    active = int(std::min<int64_t>(units, slots)) * ctas_per_unit;
   }
   const double clk_ghz = 1.8;
   const double mma_ns = 2.0 * e.bn / clk_ghz;
+  // A CTA's K block: its 128 rows of A and its share of the B rows.
   const int rows = std::min(rows_total, 128);
-  const double bytes = double(rows) * 128 + double(std::min(cols_total, e.bn)) * 128;
+  const double bytes = double(rows) * 128 + double(std::min(cols_total, e.bn)) * 128 / ctas_per_unit;
   const double hbm_gbs = 6500.0, l2_sm_gbs = 120.0;
   const double sm_gbs = std::min(l2_sm_gbs, hbm_gbs / active);
   const double load_ns = bytes / sm_gbs;
@@ -344,7 +363,7 @@ const TableEntry* balanced_entry(const TableEntry* above, int M, int N, int K, i
 Derived derive(const bfp8_gemm_problem& p, const bfp8_plan& plan) {
   const ConfigEntry& e = kConfigs[plan.config];
   Derived d;
-  d.tiles_r = cdiv(e.swap ? p.N : p.M, 128);
+  d.tiles_r = cdiv(e.swap ? p.N : p.M, e.bm);
   d.tiles_c = cdiv(e.swap ? p.M : p.N, e.bn);
   d.tiles = d.tiles_r * d.tiles_c;
   d.k_tiles = cdiv(p.K, 128);
@@ -382,7 +401,9 @@ int64_t fused_front_bytes(const bfp8_gemm_problem& p) {
 int64_t splitk_bytes(const bfp8_gemm_problem& p, const bfp8_plan& plan) {
   const Derived d = derive(p, plan);
   if (d.splits == 1) return 0;
-  return int64_t(d.splits) * d.tiles * 128 * kConfigs[plan.config].bn * int64_t(sizeof(float));
+  const ConfigEntry& e = kConfigs[plan.config];
+  // one fp32 partial per 128-row tile (a CTA pair's tile has two)
+  return int64_t(d.splits) * d.tiles * (e.bm / 128) * 128 * e.bn * int64_t(sizeof(float));
 }
 
 bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
@@ -492,8 +513,16 @@ int bfp8_plan_shape(const bfp8_gemm_problem* p, bfp8_plan plan, int* tiles, int*
   return BFP8_OK;
 }
 
+// CTA-pair configurations have no stream-K schedule.
+int check_schedule(const bfp8_plan& plan) {
+  if (plan.splits < 0 && kConfigs[plan.config].pair)
+    return fail(BFP8_EINVAL, std::string(kConfigs[plan.config].name) + " has no stream-K schedule");
+  return BFP8_OK;
+}
+
 int64_t bfp8_workspace_bytes(const bfp8_gemm_problem* p, bfp8_plan plan) {
   if (!p || !config_ok(plan.config)) return fail(BFP8_EINVAL, "bad config id");
+  if (int r = check_schedule(plan)) return r;
   if (p->M <= 0) return 0;
   const bool front = plan.fused && !quantizes_in_kernel(*p, plan);
   return (front ? fused_front_bytes(*p) : 0) + splitk_bytes(*p, plan);
@@ -501,9 +530,10 @@ int64_t bfp8_workspace_bytes(const bfp8_gemm_problem* p, bfp8_plan plan) {
 
 int bfp8_counters_needed(const bfp8_gemm_problem* p, bfp8_plan plan) {
   if (!p || !config_ok(plan.config)) return fail(BFP8_EINVAL, "bad config id");
+  if (int r = check_schedule(plan)) return r;
   if (p->M <= 0) return 0;
   const Derived d = derive(*p, plan);
-  return d.splits == 1 ? 0 : d.tiles;
+  return d.splits == 1 ? 0 : d.tiles * (kConfigs[plan.config].bm / 128);
 }
 
 int bfp8_launch_quantize(const bfp8_quant_problem* qp, void* stream) {
@@ -529,6 +559,7 @@ int bfp8_launch_gemm(const bfp8_gemm_problem* pp, bfp8_plan plan, float* workspa
   if (!pp) return fail(BFP8_EINVAL, "null problem");
   if (!config_ok(plan.config)) return fail(BFP8_EINVAL, "config out of range");
   if (plan.splits == 0) return fail(BFP8_EINVAL, "splits must be >= 1 (or negative: stream-K)");
+  if (int r = check_schedule(plan)) return r;
   bfp8_gemm_problem p = *pp;
   const bool fused = plan.fused != 0;
   if (int r = check_problem(p, fused)) return r;
@@ -571,9 +602,10 @@ int bfp8_launch_gemm(const bfp8_gemm_problem* pp, bfp8_plan plan, float* workspa
     gp.ldx = p.lda;
     gp.eps = p.eps;
   }
-  // Operand tiles: 128 rows of the MMA A operand, BN rows of the B operand,
-  // one 128-byte K block each, 128-byte swizzle.  Activations are A in the
-  // normal order and B in the swapped one.
+  // Operand tiles: 128 rows of the MMA A operand, BN rows of the B operand
+  // (a CTA pair: each CTA loads BN / 4 rows of each of the two column
+  // blocks), one 128-byte K block each, 128-byte swizzle.  Activations are A
+  // in the normal order and B in the swapped one.
   const void* a_src = e.swap ? p.b : p.a;
   const void* b_src = in_kernel ? p.b : (e.swap ? p.a : p.b);  // in-kernel: placeholder, unused
   const int64_t a_ld = e.swap ? p.ldb : p.lda, b_ld = (e.swap && !in_kernel) ? p.lda : p.ldb;
@@ -582,7 +614,7 @@ int bfp8_launch_gemm(const bfp8_gemm_problem* pp, bfp8_plan plan, float* workspa
                        uint64_t(a_rows), uint64_t(a_ld), 128, 128, CU_TENSOR_MAP_SWIZZLE_128B))
     return r;
   if (int r = make_map(&gp.map_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, b_src, uint64_t(p.K),
-                       uint64_t(b_rows), uint64_t(b_ld), 128, uint32_t(e.bn),
+                       uint64_t(b_rows), uint64_t(b_ld), 128, uint32_t(e.pair ? e.bn / 4 : e.bn),
                        CU_TENSOR_MAP_SWIZZLE_128B))
     return r;
   // Output: normal order stores [32 rows x 32 columns] chunks (64-byte
@@ -617,13 +649,14 @@ int bfp8_launch_gemm(const bfp8_gemm_problem* pp, bfp8_plan plan, float* workspa
   // sweep them all for each column tile, so A stays resident and B streams
   // from HBM once; otherwise groups of 8 row tiles (the reference's
   // group_m).  Swapped order: A is the weights, B the few token rows.
-  const int64_t a_bytes = int64_t(d.tiles_r) * 128 * p.K;
-  gp.group_r = e.swap || a_bytes <= (int64_t(48) << 20) ? d.tiles_r : 8;
+  const int64_t a_bytes = int64_t(d.tiles_r) * e.bm * p.K;
+  gp.group_r = e.swap || a_bytes <= (int64_t(48) << 20) ? d.tiles_r : 1024 / e.bm;
   gp.stream_b = (e.swap || p.M <= 128) ? 1 : 0;  // weights read once: evict them first
   gp.pdl = fused && !in_kernel ? 1 : 0;
 
   if (int r = ensure_smem_attr(plan.config, dev, in_kernel)) return r;
-  const int grid = d.sk_grid > 0 ? d.sk_grid : std::min(gp.units, sms);
+  // One CTA (a pair: two) per SM, persistent over the units.
+  const int grid = d.sk_grid > 0 ? d.sk_grid : e.pair ? 2 * std::min(gp.units, sms / 2) : std::min(gp.units, sms);
   (in_kernel ? e.launch_fused : e.launch)(gp, grid, stream);
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return cuda_fail(err, "GEMM kernel launch");

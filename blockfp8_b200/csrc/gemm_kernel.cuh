@@ -41,12 +41,24 @@
 // dependency on a previous one.
 //
 // Because every K block gets its own TMEM buffer, the MMAs of block k + 1
-// run while block k is promoted.  With split-K the units of one tile cover
-// disjoint K ranges; each writes its fp32 partial tile to a workspace and
-// the last to arrive (an atomic counter) sums the partials in split order
-// 0, 1, ..., S - 1 and stores the tile, as the reference does
-// (blockfp8 csrc/gemm_kernel.cuh:403-448): deterministic, no CTA waits for
-// another.
+// run while block k is promoted.  With two epilogue warpgroups (BN = 256) a
+// K block's MMAs go out per 128-column block, each with its own TMEM-buffer
+// barriers, so a warpgroup promotes its block while the other block's MMAs
+// still run.  With split-K the units of one tile cover disjoint K ranges;
+// each writes its fp32 partial tile to a workspace and the last to arrive
+// (an atomic counter) sums the partials in split order 0, 1, ..., S - 1 and
+// stores the tile, as the reference does (blockfp8
+// csrc/gemm_kernel.cuh:403-448): deterministic, no CTA waits for another.
+// Stream-K plans cut the tiles' K blocks into equal per-CTA ranges instead;
+// the parts of a tile meet the same way, summed in K order.
+//
+// CTA pairs (PAIR, prefill): a cluster of two CTAs computes a 256 x 256
+// tile with cta_group::2 MMAs (M = 256) issued by the leader (rank 0).  Each
+// CTA TMA-loads its own 128 A rows and 64 rows of each 128-column block of
+// B (no multicast), and holds and promotes its 128 rows of the partial sums;
+// stages and TMEM buffers are gated by the leader's barriers, and the
+// leader's commits arrive on both CTAs' barriers.  Per SM a stage is 32 KB
+// instead of 48 KB, so six stages fit.
 //
 // Every mbarrier wait is bounded (ptx.cuh): on a timeout the kernel records a
 // status code, drains its in-flight copies and MMAs, frees TMEM and returns.
@@ -86,11 +98,18 @@ struct GemmParams {
   float eps;  // in-kernel quantization: floor of each group's amax
 };
 
-template <int BN_, int STAGES_, bool SWAP_, bool FUSE_ = false>
+template <int BN_, int STAGES_, bool SWAP_, bool FUSE_ = false, bool PAIR_ = false>
 struct GemmCfg {
   static constexpr int BM = 128, BN = BN_, BK = 128, STAGES = STAGES_;
   static constexpr bool SWAP = SWAP_;
   static constexpr bool FUSE = FUSE_;
+  // PAIR: a cluster of two CTAs on a 256 x BN tile with cta_group::2 MMAs
+  // (M = 256): each CTA loads its 128 A rows and half of each B column block,
+  // holds its 128 rows of the partial sums in its TMEM and promotes them.
+  static constexpr bool PAIR = PAIR_;
+  static_assert(!PAIR || (!SWAP && !FUSE && BN == 256), "CTA pairs: normal order, 256-wide tiles");
+  static constexpr int CG = PAIR ? 2 : 1;          // tcgen05 CTA group
+  static constexpr int TILE_M = PAIR ? 256 : 128;  // MMA rows of a tile
   static_assert(SWAP ? (BN == 16 || BN == 32 || BN == 64) : (BN == 64 || BN == 128 || BN == 256),
                 "unsupported tile");
   static_assert(!FUSE || SWAP, "in-kernel quantization needs the swapped order");
@@ -118,7 +137,7 @@ struct GemmCfg {
   static constexpr int ACC_BUFS = 512 / BN > 16 ? 16 : 512 / BN;
   static constexpr int TMEM_COLS = ACC_BUFS * BN < 32 ? 32 : ACC_BUFS * BN;
   static constexpr int A_BYTES = BM * BK;
-  static constexpr int B_BYTES = BN * BK;
+  static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * BK;  // this CTA's rows of the B tile
   // FUSE: the B operand of a whole unit stays resident (ACT_KB K blocks at
   // most, 64 KB), so the ring only carries weight tiles.
   static constexpr int ACT_KB = FUSE ? 65536 / B_BYTES : 0;
@@ -130,7 +149,13 @@ struct GemmCfg {
   static constexpr int OUT_BYTES = SWAP ? BN * 64 : 2 * 32 * 64;
   static constexpr int SMEM_TILES = STAGES * STAGE_BYTES;
   static constexpr int SMEM_OUT = ((EPI_WARPS * OUT_BYTES + 1023) / 1024) * 1024;
-  static constexpr int NUM_BARS = 2 * STAGES + 2 * ACC_BUFS + 1 + ACT_KB;
+  // Each epilogue warpgroup owns a column block of the tile and its own pair
+  // of TMEM-buffer barriers; the MMAs of a K block go out per column block,
+  // so a warpgroup can promote its block while the next block's MMAs run.
+  static constexpr int COL_BLOCKS = EPI_WG;
+  static constexpr int BN_CB = BN / COL_BLOCKS;                  // MMA N of a column block
+  static constexpr int B_ROWS_CB = PAIR ? BN_CB / 2 : BN_CB;     // its B rows in this CTA
+  static constexpr int NUM_BARS = 2 * STAGES + 2 * ACC_BUFS * COL_BLOCKS + 1 + ACT_KB;
   static constexpr int ACT_RING = ACT_KB > 0 ? ACT_KB : 1;  // act_ready barriers (FUSE), at least 1 for the modulo
   static constexpr int SMEM_MISC = 16 + 4 * STAGES;  // TMEM slot, flags, last load per stage
   static constexpr int SMEM_BYTES =
@@ -179,23 +204,24 @@ __device__ __forceinline__ int sk_starts_upto(const GemmParams& p, int64_t x) {
   const int64_t n = ((x + 1) * p.sk_grid + p.sk_work - 1) / p.sk_work;
   return n < p.sk_grid ? int(n) : p.sk_grid;
 }
-__device__ __forceinline__ int first_unit(const GemmParams& p) {
-  return p.sk_grid > 0 ? int(sk_begin(p, blockIdx.x)) : int(blockIdx.x);
+// sid / scount: this CTA's (or CTA pair's) index among scount schedulers.
+__device__ __forceinline__ int first_unit(const GemmParams& p, int sid) {
+  return p.sk_grid > 0 ? int(sk_begin(p, sid)) : sid;
 }
-__device__ __forceinline__ bool unit_valid(const GemmParams& p, int u) {
-  return p.sk_grid > 0 ? u < sk_begin(p, blockIdx.x + 1) : u < p.units;
+__device__ __forceinline__ bool unit_valid(const GemmParams& p, int u, int sid) {
+  return p.sk_grid > 0 ? u < sk_begin(p, sid + 1) : u < p.units;
 }
 
 // Tiles are rasterised in groups of group_r row tiles, row tiles fastest
 // inside a group (the reference's order, blockfp8
 // csrc/gemm_kernel.cuh:120-125); the host picks group_r so the operand that
 // is re-read stays in L2.
-__device__ __forceinline__ UnitCoord unit_coord(const GemmParams& p, int u) {
+__device__ __forceinline__ UnitCoord unit_coord(const GemmParams& p, int u, int sid) {
   UnitCoord c;
   if (p.sk_grid > 0) {
     c.tile = u / p.k_tiles;
     c.kt0 = u % p.k_tiles;
-    const int64_t end = c.kt0 + (sk_begin(p, blockIdx.x + 1) - u);
+    const int64_t end = c.kt0 + (sk_begin(p, sid + 1) - u);
     c.kt1 = end < p.k_tiles ? int(end) : p.k_tiles;
     const int64_t t0 = int64_t(c.tile) * p.k_tiles;
     const int before = sk_starts_upto(p, t0);
@@ -216,8 +242,8 @@ __device__ __forceinline__ UnitCoord unit_coord(const GemmParams& p, int u) {
   return c;
 }
 
-__device__ __forceinline__ int next_unit(const GemmParams& p, int u, const UnitCoord& c) {
-  return p.sk_grid > 0 ? c.tile * p.k_tiles + c.kt1 : u + int(gridDim.x);
+__device__ __forceinline__ int next_unit(const GemmParams& p, int u, const UnitCoord& c, int scount) {
+  return p.sk_grid > 0 ? c.tile * p.k_tiles + c.kt1 : u + scount;
 }
 
 template <int N>
@@ -346,7 +372,8 @@ __device__ __forceinline__ void quantize_unit(const GemmParams& p, const UnitCoo
 template <class Cfg>
 __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_constant__ GemmParams p) {
   constexpr int BN = Cfg::BN, STAGES = Cfg::STAGES, ACC_BUFS = Cfg::ACC_BUFS, COLS = Cfg::COLS;
-  constexpr bool SWAP = Cfg::SWAP, FUSE = Cfg::FUSE;
+  constexpr bool SWAP = Cfg::SWAP, FUSE = Cfg::FUSE, PAIR = Cfg::PAIR;
+  constexpr int CG = Cfg::CG;
   constexpr int PF = 4;  // scale prefetch distance in K blocks
 
   extern __shared__ uint8_t smem_raw[];
@@ -360,26 +387,38 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
   const uint32_t s_bars = s_act_scales + Cfg::SMEM_ACT_SCALES;
   auto full = [&](int s) { return s_bars + 8u * s; };
   auto empty = [&](int s) { return s_bars + 8u * (STAGES + s); };
-  auto acc_full = [&](int a) { return s_bars + 8u * (2 * STAGES + a); };
-  auto acc_empty = [&](int a) { return s_bars + 8u * (2 * STAGES + ACC_BUFS + a); };
-  const uint32_t mma_done = s_bars + 8u * (2 * STAGES + 2 * ACC_BUFS);
-  const uint32_t act_ready0 = s_bars + 8u * (2 * STAGES + 2 * ACC_BUFS + 1);  // FUSE: [ACT_KB], by position
+  constexpr int CB = Cfg::COL_BLOCKS;
+  auto acc_full = [&](int a, int h) { return s_bars + 8u * (2 * STAGES + a * CB + h); };
+  auto acc_empty = [&](int a, int h) { return s_bars + 8u * (2 * STAGES + (ACC_BUFS + a) * CB + h); };
+  const uint32_t mma_done = s_bars + 8u * (2 * STAGES + 2 * ACC_BUFS * CB);
+  const uint32_t act_ready0 = mma_done + 8u;  // FUSE: [ACT_KB], by position
   uint32_t* misc = reinterpret_cast<uint32_t*>(smem + (s_bars - base) + 8 * Cfg::NUM_BARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 1);
   volatile int* last_flag = reinterpret_cast<volatile int*>(misc + 2);
   volatile int* stage_seq = reinterpret_cast<volatile int*>(misc + 4);  // last K block loaded per stage
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // Scheduling: a CTA pair walks the units together (cluster rank 0 leads:
+  // its barriers gate the stages and TMEM buffers, its thread issues the MMAs).
+  const uint32_t rank = PAIR ? cluster_rank() : 0u;
+  const bool leader = rank == 0;
+  const int sid = PAIR ? int(blockIdx.x >> 1) : int(blockIdx.x);
+  const int scount = PAIR ? int(gridDim.x >> 1) : int(gridDim.x);
+  const int row_off = PAIR ? int(rank) * 128 : 0;  // this CTA's first row inside a tile
+  // The leader's copy of one of this CTA's barriers (same offset).
+  auto leader_bar = [&](uint32_t bar) { return PAIR ? map_shared_rank(bar, 0) : bar; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(full(s), 1);
       mbar_init(empty(s), 1);
     }
-    for (int a = 0; a < ACC_BUFS; ++a) {
-      mbar_init(acc_full(a), 1);
-      mbar_init(acc_empty(a), Cfg::EPI_WARPS);
-    }
+    for (int a = 0; a < ACC_BUFS; ++a)
+      for (int h = 0; h < CB; ++h) {
+        mbar_init(acc_full(a, h), 1);
+        // the four warps of column block h's warpgroup (of both CTAs of a pair)
+        mbar_init(acc_empty(a, h), PAIR ? 8 : 4);
+      }
     mbar_init(mma_done, 2);  // one commit from each MMA issuer
     for (int k = 0; k < Cfg::ACT_KB; ++k) mbar_init(act_ready0 + 8u * k, 1);  // FUSE: activations in place
     *abort_flag = 0;
@@ -392,11 +431,12 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
     tma_prefetch_desc(&p.map_c);
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(misc), Cfg::TMEM_COLS);
-    tmem_relinquish();
+    tmem_alloc<CG>(smem_u32(misc), Cfg::TMEM_COLS);
+    tmem_relinquish<CG>();
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // the peer's barriers are initialised before any remote use
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = misc[0];
 
@@ -427,20 +467,38 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
         const CUtensorMap* map_x = SWAP ? &p.map_b : &p.map_a;
         const uint32_t off_w = SWAP ? 0u : uint32_t(Cfg::A_BYTES);
         const uint32_t off_x = SWAP ? uint32_t(Cfg::A_BYTES) : 0u;
-        constexpr uint32_t kFullBytes = Cfg::STAGE_BYTES;
+        // A pair's stage completes on the leader's barrier with both CTAs' bytes.
+        constexpr uint32_t kFullBytes = Cfg::STAGE_BYTES * (PAIR ? 2 : 1);
         auto w_row = [&](const UnitCoord& c) { return SWAP ? c.tr * 128 : c.tc * BN; };
-        auto x_row = [&](const UnitCoord& c) { return SWAP ? c.tc * BN : c.tr * 128; };
+        auto x_row = [&](const UnitCoord& c) { return SWAP ? c.tc * BN : c.tr * Cfg::TILE_M + row_off; };
+        // Weight tile of a K block: the BN rows, or for a pair this CTA's
+        // B_ROWS_CB-row share of each column block (rows h * BN_CB + rank * B_ROWS_CB).
+        auto load_w = [&](uint32_t dst, int kt, const UnitCoord& c, int stage, uint64_t pol) {
+          if constexpr (PAIR) {
+#pragma unroll
+            for (int h = 0; h < CB; ++h)
+              tma_load_2d_pair(dst + off_w + uint32_t(h * Cfg::B_ROWS_CB * 128), map_w, kt * 128,
+                               w_row(c) + h * Cfg::BN_CB + int(rank) * Cfg::B_ROWS_CB, leader_bar(full(stage)),
+                               pol);
+          } else {
+            tma_load_2d(dst + off_w, map_w, kt * 128, w_row(c), full(stage), pol);
+          }
+        };
+        auto load_x = [&](uint32_t dst, int kt, const UnitCoord& c, int stage, uint64_t pol) {
+          if constexpr (PAIR) tma_load_2d_pair(dst + off_x, map_x, kt * 128, x_row(c), leader_bar(full(stage)), pol);
+          else tma_load_2d(dst + off_x, map_x, kt * 128, x_row(c), full(stage), pol);
+        };
         int early = 0;  // K blocks (of the whole sequence) whose weights went out early
         if (p.pdl && !FUSE) {
           int seq = 0;
-          for (int u = first_unit(p); unit_valid(p, u) && seq < STAGES;) {
-            const UnitCoord c = unit_coord(p, u);
-            u = next_unit(p, u, c);
+          for (int u = first_unit(p, sid); unit_valid(p, u, sid) && seq < STAGES;) {
+            const UnitCoord c = unit_coord(p, u, sid);
+            u = next_unit(p, u, c, scount);
             for (int kt = c.kt0; kt < c.kt1 && seq < STAGES; ++kt, ++seq) {
               if ((seq & 1) != role) continue;
               const uint32_t dst = s_tiles + uint32_t(seq) * Cfg::STAGE_BYTES;  // stage = seq
-              mbar_arrive_expect_tx(full(seq), kFullBytes);
-              tma_load_2d(dst + off_w, map_w, kt * 128, w_row(c), full(seq), pol_wgt);
+              if (leader) mbar_arrive_expect_tx(full(seq), kFullBytes);
+              load_w(dst, kt, c, seq, pol_wgt);
               stage_seq[seq] = seq;
             }
           }
@@ -449,15 +507,15 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
         if (!FUSE) griddep_wait();  // activations are the previous kernel's output
         int seq = 0;
         bool ok = true;
-        for (int u = first_unit(p); ok && unit_valid(p, u);) {
-          const UnitCoord c = unit_coord(p, u);
-          u = next_unit(p, u, c);
+        for (int u = first_unit(p, sid); ok && unit_valid(p, u, sid);) {
+          const UnitCoord c = unit_coord(p, u, sid);
+          u = next_unit(p, u, c, scount);
           for (int kt = c.kt0; kt < c.kt1; ++kt, ++seq) {
             if ((seq & 1) != role) continue;
             const int stage = seq % STAGES;
             const uint32_t dst = s_tiles + uint32_t(stage) * Cfg::STAGE_BYTES;
             if (seq < early) {  // weights already requested; add the activations
-              tma_load_2d(dst + off_x, map_x, kt * 128, x_row(c), full(stage), pol_act);
+              load_x(dst, kt, c, stage, pol_act);
               continue;
             }
             const uint32_t phase = uint32_t(seq / STAGES) & 1u;
@@ -465,15 +523,22 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
               ok = false;
               break;
             }
-            mbar_arrive_expect_tx(full(stage), kFullBytes);
-            tma_load_2d(dst + off_w, map_w, kt * 128, w_row(c), full(stage), pol_wgt);
-            if constexpr (!FUSE) tma_load_2d(dst + off_x, map_x, kt * 128, x_row(c), full(stage), pol_act);
+            if (leader) mbar_arrive_expect_tx(full(stage), kFullBytes);
+            load_w(dst, kt, c, stage, pol_wgt);
+            if constexpr (!FUSE) load_x(dst, kt, c, stage, pol_act);
             stage_seq[stage] = seq;
           }
         }
-      } else {
+      } else if (leader) {
         // ------------------------------------------------------------ MMA issuer
-        constexpr uint32_t idesc = idesc_e4m3_f32(128, BN);
+        // (a pair's MMAs are issued by the leader for both CTAs)
+        constexpr int BN_CB = Cfg::BN_CB;
+        constexpr uint32_t idesc = idesc_e4m3_f32(Cfg::TILE_M, BN_CB);
+        // Commits arrive on this CTA's barrier and, for a pair, on the peer's.
+        auto commit_both = [&](uint32_t bar) {
+          mma_commit<CG>(bar);
+          if constexpr (PAIR) mma_commit<CG>(map_shared_rank(bar, 1));
+        };
         // Descriptors of stage 0's tiles; a stage, a resident K block or a K
         // step only moves the 14-bit start-address field (16-byte units),
         // which never carries out (shared memory ends below 256 KB).
@@ -481,9 +546,9 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
         const uint64_t desc_b0 = smem_desc_k128_sw128(FUSE ? s_act : s_tiles + Cfg::A_BYTES);
         int seq = 0;
         bool ok = true;
-        for (int u = first_unit(p); ok && unit_valid(p, u);) {
-          const UnitCoord c = unit_coord(p, u);
-          u = next_unit(p, u, c);
+        for (int u = first_unit(p, sid); ok && unit_valid(p, u, sid);) {
+          const UnitCoord c = unit_coord(p, u, sid);
+          u = next_unit(p, u, c, scount);
           for (int kt = c.kt0; kt < c.kt1; ++kt, ++seq) {
             if ((seq & 1) != role) continue;
             if (FUSE && !mbar_wait(act_ready0 + 8u * uint32_t(seq % Cfg::ACT_RING),
@@ -494,24 +559,34 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
             const int stage = seq % STAGES, acc = seq % ACC_BUFS;
             const uint32_t phase = uint32_t(seq / STAGES) & 1u;
             const uint32_t acc_phase = uint32_t(seq / ACC_BUFS) & 1u;
-            if (!mbar_wait(acc_empty(acc), acc_phase ^ 1u, abort_flag, kWaitAccEmpty) ||
-                !mbar_wait(full(stage), phase, abort_flag, kWaitFull)) {
+            if (!mbar_wait(full(stage), phase, abort_flag, kWaitFull)) {
               ok = false;
               break;
             }
-            tc_fence_after();
             const uint64_t a_off = uint64_t(stage) * (Cfg::STAGE_BYTES >> 4);
             const uint64_t b_off = FUSE ? uint64_t(kt - c.kt0) * (Cfg::B_BYTES >> 4) : a_off;
-            const uint32_t d = tmem_base + uint32_t(acc * BN);
 #pragma unroll
-            for (int k = 0; k < 4; ++k)  // K step of 32 e4m3 = 32 bytes = 2 descriptor units
-              mma_f8(d, desc_a0 + a_off + 2 * k, desc_b0 + b_off + 2 * k, idesc, k > 0 ? 1u : 0u);
-            mma_commit(empty(stage));   // the smem stage is free once these MMAs are done
-            mma_commit(acc_full(acc));  // ... and the partial sums are in TMEM
+            for (int h = 0; h < CB; ++h) {
+              if (!mbar_wait(acc_empty(acc, h), acc_phase ^ 1u, abort_flag, kWaitAccEmpty)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              // Column block h: TMEM columns acc * BN + h * BN_CB; its B rows
+              // start B_ROWS_CB * h rows into the stage's B tile (128 bytes a row).
+              const uint32_t d = tmem_base + uint32_t(acc * BN + h * BN_CB);
+              const uint64_t bh = uint64_t(h) * ((Cfg::B_ROWS_CB * 128) >> 4);
+#pragma unroll
+              for (int k = 0; k < 4; ++k)  // K step of 32 e4m3 = 32 bytes = 2 descriptor units
+                mma_f8<CG>(d, desc_a0 + a_off + 2 * k, desc_b0 + b_off + bh + 2 * k, idesc, k > 0 ? 1u : 0u);
+              commit_both(acc_full(acc, h));  // column block h's partial sums are in TMEM
+            }
+            if (!ok) break;
+            commit_both(empty(stage));  // the smem stage is free once these MMAs are done
           }
         }
         // All MMAs of both issuers complete before TMEM is freed.
-        mma_commit(mma_done);
+        mma_commit<CG>(mma_done);
         mbar_wait(mma_done, 0, nullptr, kWaitMmaDone);
       }
     }
@@ -521,7 +596,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
       // the MMA threads have seen them all; after an abort, wait on the last
       // load of each stage (its phase completes when its bytes arrive).
       named_bar_sync(2, 64);  // both producers are done issuing
-      if (warp == 0 && lane == 0)
+      // (a pair's stages complete on the leader's barriers, with both CTAs' bytes)
+      if (warp == 0 && lane == 0 && leader)
         for (int st = 0; st < STAGES; ++st)
           if (stage_seq[st] >= 0)
             mbar_wait(full(st), uint32_t(stage_seq[st] / STAGES) & 1u, nullptr, kWaitDrain);
@@ -543,9 +619,10 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
     int out_chunk = 0;  // normal mode: alternates between the two staging buffers
 
     // Scale sources of a unit.  Normal: sa per row (thread), sb per
-    // 128-column block (warpgroup).  Swapped: sb per 128-row tile (CTA), sa
-    // per token column; lane j loads token col0 + j (and col0 + 32 + j when
-    // BN = 64).  FUSE: sa comes from the unit's resident scales.
+    // 128-column block (warpgroup g promotes column block g).  Swapped: sb per
+    // 128-row tile (CTA), sa per token column; lane j loads token col0 + j
+    // (and col0 + 32 + j when BN = 64).  FUSE: sa comes from the unit's
+    // resident scales.
     struct ScaleSrc {
       const float* sa;
       const float* sa2;
@@ -556,7 +633,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
       ScaleSrc q{p.sa, p.sa, p.sb, false, false, false};
       const int col0 = c.tc * BN + g * COLS;
       if constexpr (!SWAP) {
-        const int r = c.tr * 128 + row;
+        const int r = c.tr * Cfg::TILE_M + row_off + row;
         q.sa_ok = r < rows_total;
         q.sa = p.sa + int64_t(q.sa_ok ? r : 0) * p.sa_m;
         q.sb_ok = col0 < p.N;
@@ -599,28 +676,29 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
     };
 
     if (!FUSE) griddep_wait();  // activation scales are the previous kernel's output
-    const int u0 = first_unit(p);
-    const bool any_unit = unit_valid(p, u0);
-    UnitCoord c_next = unit_coord(p, any_unit ? u0 : 0);
+    const int u0 = first_unit(p, sid);
+    const bool any_unit = unit_valid(p, u0, sid);
+    UnitCoord c_next = unit_coord(p, any_unit ? u0 : 0, sid);
     if (any_unit) {
       prefetch_unit(c_next, pa, pa2, pb);
       publish_unit(c_next, 0);
     }
 
     int next_seq = 0;  // position of the next unit's first K block in the CTA's sequence
-    for (int u = u0; any_unit && unit_valid(p, u);) {
+    for (int u = u0; any_unit && unit_valid(p, u, sid);) {
       const UnitCoord c = c_next;
-      u = next_unit(p, u, c);
+      u = next_unit(p, u, c, scount);
       next_seq += c.kt1 - c.kt0;
       const ScaleSrc src = scale_src(c);
-      const bool more = unit_valid(p, u);
+      const bool more = unit_valid(p, u, sid);
       if (more) {
-        c_next = unit_coord(p, u);
+        c_next = unit_coord(p, u, sid);
         prefetch_unit(c_next, na, na2, nb);
       }
-      const int r = c.tr * 128 + row;                       // this thread's MMA row
+      const int row0 = c.tr * Cfg::TILE_M + row_off;       // this CTA's first row of the tile
+      const int r = row0 + row;                             // this thread's MMA row
       const bool row_ok = r < rows_total;
-      const bool warp_rows = c.tr * 128 + 32 * quarter < rows_total;  // warp-uniform
+      const bool warp_rows = row0 + 32 * quarter < rows_total;  // warp-uniform
       const int col0 = c.tc * BN + g * COLS;                // first MMA column of this thread
       const int cols_total = SWAP ? p.M : p.N;
       const bool cols_ok = col0 < cols_total;               // warp-uniform
@@ -644,21 +722,50 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
               sa_v = lane < BN ? ld_shared_f32(sl + uint32_t(lane) * 4u) : 0.f;
               if constexpr (BN > 32) sa2_v = ld_shared_f32(sl + uint32_t(32 + lane) * 4u);
             }
-            ok = mbar_wait(acc_full(acc), acc_phase, abort_flag, kWaitAccFull) && ok;
-            tc_fence_after();
-            if (work) {
-              const uint32_t t = t_lane + uint32_t(acc * BN + g * COLS);
-              if constexpr (!SWAP) {
-                // One scale per thread: sa[row] * sb[block], as the reference forms it.
+            // This warp's release of TMEM buffer acc's column block h.
+            auto release = [&](int h) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) {
+                if constexpr (PAIR) mbar_arrive_cluster(leader_bar(acc_empty(acc, h)));
+                else mbar_arrive(acc_empty(acc, h));
+              }
+            };
+            if constexpr (!SWAP) {
+              // Warpgroup g promotes column block g.  One scale per thread:
+              // sa[row] * sb[block], as the reference forms it; 32-column
+              // chunks loaded two at a time, promoted with packed fmas (each
+              // lane of fma.rn.f32x2 rounds like fmaf); then the buffer's
+              // block goes back to the MMA issuer.
+              ok = mbar_wait(acc_full(acc, g), acc_phase, abort_flag, kWaitAccFull) && ok;
+              tc_fence_after();
+              if (work) {
+                const uint32_t t = t_lane + uint32_t(acc * BN + g * COLS);
                 const float scale = sa_v * sb_v;
 #pragma unroll
-                for (int ch = 0; ch < COLS / 32; ++ch) {
-                  float part[32];
-                  tmem_ld<32>(t + 32 * ch, part);
+                for (int ch = 0; ch < COLS / 32; ch += 2) {
+                  uint32_t r0[32], r1[32];
+                  tmem_ld32_async(t + 32 * ch, r0);
+                  if (ch + 1 < COLS / 32) tmem_ld32_async(t + 32 * (ch + 1), r1);
+                  tmem_wait_ld();
 #pragma unroll
-                  for (int i = 0; i < 32; ++i) accum[32 * ch + i] = fmaf(part[i], scale, accum[32 * ch + i]);
+                  for (int i = 0; i < 32; i += 2)
+                    fma2(accum[32 * ch + i], accum[32 * ch + i + 1], __uint_as_float(r0[i]),
+                         __uint_as_float(r0[i + 1]), scale, scale);
+                  if (ch + 1 < COLS / 32) {
+#pragma unroll
+                    for (int i = 0; i < 32; i += 2)
+                      fma2(accum[32 * (ch + 1) + i], accum[32 * (ch + 1) + i + 1], __uint_as_float(r1[i]),
+                           __uint_as_float(r1[i + 1]), scale, scale);
+                  }
                 }
-              } else {
+              }
+              release(g);
+            } else {
+              ok = mbar_wait(acc_full(acc, 0), acc_phase, abort_flag, kWaitAccFull) && ok;
+              tc_fence_after();
+              if (work) {
+                const uint32_t t = t_lane + uint32_t(acc * BN);
                 constexpr int CH = BN < 32 ? BN : 32;
 #pragma unroll
                 for (int ch = 0; ch < BN / CH; ++ch) {
@@ -666,16 +773,15 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
                   tmem_ld<CH>(t + CH * ch, part);
                   const float src_s = ch == 0 ? sa_v : sa2_v;
 #pragma unroll
-                  for (int i = 0; i < CH; ++i) {
-                    const float scale = __shfl_sync(0xffffffffu, src_s, i) * sb_v;
-                    accum[CH * ch + i] = fmaf(part[i], scale, accum[CH * ch + i]);
+                  for (int i = 0; i < CH; i += 2) {
+                    const float s0 = __shfl_sync(0xffffffffu, src_s, i) * sb_v;
+                    const float s1 = __shfl_sync(0xffffffffu, src_s, i + 1) * sb_v;
+                    fma2(accum[CH * ch + i], accum[CH * ch + i + 1], part[i], part[i + 1], s0, s1);
                   }
                 }
               }
+              release(0);
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(acc_empty(acc));
             if (++acc == ACC_BUFS) {
               acc = 0;
               acc_phase ^= 1u;
@@ -705,8 +811,10 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
       if (c.pieces > 1) {
         // Deterministic split-K: publish this split's partial, count arrivals;
         // the last CTA of the tile sums all partials in split order.
-        const int64_t split_stride = int64_t(p.tiles) * (128 * BN);
-        float* ws_tile = p.workspace + int64_t(c.tile) * (128 * BN);
+        // Partials per 128-row tile half (a pair's CTAs hand off separately).
+        const int wtile = PAIR ? c.tile * 2 + int(rank) : c.tile;
+        const int64_t split_stride = int64_t(p.tiles) * (PAIR ? 2 : 1) * (128 * BN);
+        float* ws_tile = p.workspace + int64_t(wtile) * (128 * BN);
         if (row_ok && cols_ok && ok) {
           if constexpr (!SWAP) {
             float* w = ws_tile + c.split * split_stride + row * BN + g * COLS;
@@ -725,7 +833,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
         // makes the other parts' partials visible to the last arriver.
         named_bar_sync(1, Cfg::EPI_THREADS);
         if (ew == 0 && lane == 0)
-          *last_flag = atom_add_acq_rel_gpu(p.counters + c.tile, 1) == c.pieces - 1;
+          *last_flag = atom_add_acq_rel_gpu(p.counters + wtile, 1) == c.pieces - 1;
         named_bar_sync(1, Cfg::EPI_THREADS);
         const bool last = *last_flag != 0;
         store = store && last;
@@ -754,7 +862,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
               }
             }
           }
-          if (ew == 0 && lane == 0) p.counters[c.tile] = 0;  // ready for the next launch
+          if (ew == 0 && lane == 0) p.counters[wtile] = 0;  // ready for the next launch
         }
       }
 
@@ -764,7 +872,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
           // turn so one chunk's TMA store overlaps the next chunk's writes.
 #pragma unroll
           for (int ch = 0; ch < COLS / 32; ++ch) {
-            if (col0 + 32 * ch >= p.N) break;
+            const int col = col0 + 32 * ch;
+            if (col >= p.N) break;
             const uint32_t buf = out_buf + uint32_t(out_chunk) * 2048u;
             if (lane == 0) bulk_wait_read1();  // the store that last read this buffer is done
             __syncwarp();
@@ -778,7 +887,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-              tma_store_2d(&p.map_c, col0 + 32 * ch, c.tr * 128 + 32 * quarter, buf);
+              tma_store_2d(&p.map_c, col, row0 + 32 * quarter, buf);
               bulk_commit();
             }
             out_chunk ^= 1;
@@ -804,10 +913,14 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
   }
 
   tc_fence_before();
-  __syncthreads();
+  // A pair: the leader's MMAs (which read this CTA's tiles and write its
+  // TMEM) and both CTAs' remote arrivals are over before either frees
+  // TMEM or exits.
+  if constexpr (PAIR) cluster_sync();
+  else __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+    tmem_dealloc<CG>(tmem_base, Cfg::TMEM_COLS);
   }
 }
 

@@ -126,7 +126,10 @@ def test_both_fused_modes_equal_the_quantized_gemm(m, n, k, splits):
     x = bf16_activations(m, k, seed=7 + m, ties=True).to(DEV)
     q, s = capi.quantize(x)
     lib = _native.capi()
+    names = [lib.bfp8_config_name(i).decode() for i in range(lib.bfp8_num_configs())]
     for config in range(lib.bfp8_num_configs()):
+        if splits < 0 and names[config].startswith("m256"):
+            continue  # CTA pairs have no stream-K schedule
         expect = capi.gemm(q, s, b, sb, config=config, splits=splits)
         for mode in (1, 2):
             got = capi.gemm(x, None, b, sb, config=config, splits=splits, fused=mode)
