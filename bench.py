@@ -331,6 +331,11 @@ def profile_case(spec):
     print(json.dumps({"profile_case": spec, "ok": True}))
 
 
+# DRAM bytes (read + write) of one headline GEMM launch at N = 1, from one ncu
+# capture (profiles/gemm_kernel_gate_up_m8192_dram.md).
+HEADLINE_TRAFFIC = 187.65e6 + 379.59e6
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -418,7 +423,10 @@ def main():
                          "unit": "TFLOP/s", "frac": round(gemm_tflops / fp8_peak, 4),
                          "peak_source": f"2 x bf16_tflops of MEASURED_PEAKS.json ({pk['source']}): "
                                         "dense e4m3 runs at twice the bf16 rate",
-                         "traffic": None,
+                         "traffic": HEADLINE_TRAFFIC if (world == 1 and (m, n_per, k) == (8192, 24576, 4096))
+                         else None,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one headline "
+                                           "launch (profiles/gemm_kernel_gate_up_m8192_dram.md); N = 1 only",
                          "algorithmic": f"2*M*N*K = {fp8_gemm_flops(m, n_per, k):.4g} FLOP per launch"},
             "breakdown_us": {"quantize": round(quant_us, 2), "gemm_mean": round(gemm_us, 2),
                              "gemm_median": round(gemm_med, 2), "linear_mean": round(mine * 1e3, 2)},
