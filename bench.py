@@ -226,17 +226,29 @@ def cpu_step(O, xbits, b, sb):
 
 
 def cpu_threads():
-    return int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    """Host CPUs this process may use (all of them for the CPU legs, whatever
+    OMP_NUM_THREADS torchrun set for the GPU ranks)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def all_host_threads():
+    """OpenMP (the C oracle) and BLAS (numpy) pools at cpu_threads() threads."""
+    from threadpoolctl import threadpool_limits
+    return threadpool_limits(limits=cpu_threads())
 
 
 def run_cpu_baseline(rows=REF_SAMPLE_ROWS, reps=2):
     O, xbits, b, sb, n, k = cpu_sample(rows)
-    cpu_step(O, xbits, b, sb)  # warm (BLAS threads, page faults)
-    t = []
-    for _ in range(reps):
-        t0 = time.perf_counter()
-        cpu_step(O, xbits, b, sb)
-        t.append(time.perf_counter() - t0)
+    with all_host_threads():
+        cpu_step(O, xbits, b, sb)  # warm (BLAS threads, page faults)
+        t = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            cpu_step(O, xbits, b, sb)
+            t.append(time.perf_counter() - t0)
     sec = statistics.median(t)
     return {"value": 2 * rows * n * k / sec / 1e12, "unit": "TFLOPS", "cores": cpu_threads(),
             "kind": "port",
@@ -251,12 +263,13 @@ def run_reference(args):
     if rank != 0:
         return 0
     O, xbits, b, sb, n, k = cpu_sample(REF_SAMPLE_ROWS)
-    for _ in range(max(1, args.warmup)):
-        cpu_step(O, xbits, b, sb)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        cpu_step(O, xbits, b, sb)
-    sec = (time.perf_counter() - t0) / args.steps
+    with all_host_threads():
+        for _ in range(max(1, args.warmup)):
+            cpu_step(O, xbits, b, sb)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            cpu_step(O, xbits, b, sb)
+        sec = (time.perf_counter() - t0) / args.steps
     value = 2 * REF_SAMPLE_ROWS * n * k / sec / 1e12
     name, m = HEADLINE
     line = {

@@ -62,7 +62,7 @@ def row_parallel_linear(x: torch.Tensor, b_q: torch.Tensor, b_scales: torch.Tens
     """linear on this rank's K slice, then a sum all-reduce of the [M, N] partials."""
     import torch.distributed as dist
 
-    from . import gemm as _gemm
-    y = _gemm.linear(x.contiguous(), b_q.contiguous(), b_scales.contiguous())
+    from .gemm import linear  # the submodule's function (the package re-exports a `gemm` function)
+    y = linear(x.contiguous(), b_q.contiguous(), b_scales.contiguous())
     dist.all_reduce(y, op=dist.ReduceOp.SUM, group=group)
     return y

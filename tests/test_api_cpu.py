@@ -255,3 +255,14 @@ def test_fake_kernels_give_the_output_layouts():
         assert q.shape == (5, 256) and q.dtype == FP8 and s.shape == (5, 2) and s.stride() == (1, 5)
         assert torch.ops.blockfp8.linear(x, b, sb).shape == (5, 128)
         assert torch.ops.blockfp8.gemm_bf16(x, b, sb, -1, 0, 1e-10).dtype == torch.bfloat16
+
+
+def test_row_parallel_linear_resolves_the_linear_function():
+    """row_parallel_linear calls the API's linear (the package's `gemm`
+    attribute is the gemm function, not the submodule)."""
+    import inspect
+    from blockfp8_b200 import gemm as gemm_attr, sharding
+    from blockfp8_b200.gemm import linear
+    assert callable(gemm_attr) and not inspect.ismodule(gemm_attr)
+    src = inspect.getsource(sharding.row_parallel_linear)
+    assert "from .gemm import linear" in src and callable(linear)

@@ -109,7 +109,8 @@ def _row_worker(rank, world, port, out):
 
 def _run(worker, world=2):
     port = _free_port()
-    with mp.Manager() as mgr:
+    # spawn, not fork: the test process may already hold a CUDA context
+    with mp.get_context("spawn").Manager() as mgr:
         out = mgr.dict()
         mp.spawn(worker, args=(world, port, out), nprocs=world, join=True)
         return dict(out)
@@ -138,7 +139,7 @@ def _dying_worker(rank, world, port, out):
 
 def test_a_dead_rank_is_noticed_by_a_timeout_not_a_hang():
     port = _free_port()
-    with mp.Manager() as mgr:
+    with mp.get_context("spawn").Manager() as mgr:
         out = mgr.dict()
         ctx = mp.get_context("spawn")
         procs = [ctx.Process(target=_dying_worker, args=(r, 2, port, out)) for r in range(2)]
