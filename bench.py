@@ -329,6 +329,28 @@ def sweeps(dev, calls=48):
     return out
 
 
+def run_probes(dev, gemm_tflops, sweeps_out):
+    """Same-session roofline probes on this GPU (libblockfp8_b200's
+    bfp8_probe_*): the dense e4m3 tensor-core rate with no operand traffic,
+    and the HBM read rate; the headline GEMM and the decode sweep against
+    them.  The roofline object above keeps MEASURED_PEAKS.json's figures."""
+    from blockfp8_b200 import _native
+    tf, mpc = _native.probe_mma(256, 4000)
+    buf = torch.empty(4 << 30, dtype=torch.uint8, device=dev)
+    gbs = _native.probe_hbm_read(buf, reps=5)
+    del buf
+    torch.cuda.empty_cache()
+    out = {"fp8_mma_tflops": round(tf, 1), "fp8_mma_macs_per_clock_per_sm": round(mpc, 1),
+           "hbm_read_gbs": round(gbs, 1),
+           "headline_gemm_frac_of_mma_probe": round(gemm_tflops / tf, 4),
+           "how": "bfp8_probe_mma: 128x256x32 tcgen05 e4m3 MMAs back to back from shared memory on every "
+                  "SM; bfp8_probe_hbm_read: streaming 16-byte reads of a 4 GiB buffer"}
+    if sweeps_out:
+        dec = [v["weight_gbs"] for k_, v in sweeps_out["decode"].items() if int(k_.split("_m")[1]) <= 16]
+        out["decode_m_le_16_median_frac_of_read_probe"] = round(statistics.median(dec) / gbs, 4)
+    return out
+
+
 def profile_case(spec):
     """A few launches of one case, for ncu (no timing printed)."""
     import blockfp8_b200 as bf
@@ -462,6 +484,7 @@ def main():
                 "min_frac_m_le_16": round(min(v["weight_gbs"] for v in best.values()) / pk["hbm_gbs"], 3),
                 "median_frac_m_le_16": round(statistics.median(v["weight_gbs"] for v in best.values())
                                              / pk["hbm_gbs"], 3)}
+        line["probes"] = run_probes(dev, gemm_tflops, line.get("sweeps"))
         if not args.no_cpu:
             line["cpu_baseline"] = run_cpu_baseline()
     if rank == 0:

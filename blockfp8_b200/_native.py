@@ -72,6 +72,10 @@ _SIGNATURES = {
     "bfp8_launch_gemm_noalloc": ([ctypes.POINTER(GemmProblem), Plan, ctypes.c_void_p], ctypes.c_int),
     "bfp8_launch_quantize": ([ctypes.POINTER(QuantProblem), ctypes.c_void_p], ctypes.c_int),
     "bfp8_device_status": ([ctypes.c_int], ctypes.c_int64),
+    "bfp8_probe_mma": ([ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_double),
+                        ctypes.POINTER(ctypes.c_double)], ctypes.c_int),
+    "bfp8_probe_hbm_read": ([ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.POINTER(ctypes.c_double)],
+                            ctypes.c_int),
 }
 
 _capi = None
@@ -144,3 +148,19 @@ def device_status(reset: bool = False) -> int:
     v = capi().bfp8_device_status(1 if reset else 0)
     check(v if v < 0 else 0)
     return v
+
+
+def probe_mma(n: int = 256, iters: int = 2000) -> tuple[float, float]:
+    """(TFLOP/s, multiply-adds per clock per SM) of back-to-back 128 x n x 32
+    e4m3 tcgen05 MMAs on every SM of the current device."""
+    tf, mpc = ctypes.c_double(), ctypes.c_double()
+    check(capi().bfp8_probe_mma(n, iters, ctypes.byref(tf), ctypes.byref(mpc)))
+    return tf.value, mpc.value
+
+
+def probe_hbm_read(buf, reps: int = 5) -> float:
+    """GB/s of a streaming read of the device tensor `buf` (use more than L2)."""
+    gbs = ctypes.c_double()
+    check(capi().bfp8_probe_hbm_read(ctypes.c_void_p(buf.data_ptr()), buf.numel() * buf.element_size(), reps,
+                                     ctypes.byref(gbs)))
+    return gbs.value

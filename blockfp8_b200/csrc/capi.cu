@@ -20,7 +20,11 @@
 
 #include "blockfp8_b200.h"
 
+#include <algorithm>
+#include <vector>
+
 #include "gemm_kernel.cuh"
+#include "probes.cuh"
 #include "quantize.cuh"
 
 namespace bfp8 {
@@ -708,3 +712,78 @@ int64_t bfp8_device_status(int reset) {
 }
 
 }  // extern "C"
+
+// ---- roofline probes (no reference counterpart) ------------------------------------
+
+namespace {
+
+template <int N>
+int run_probe_mma(int iters, double* tflops, double* macs_per_clock) {
+  using namespace bfp8;
+  const int sms = current_device_sms(nullptr);
+  if (sms <= 0) return cuda_fail(cudaGetLastError(), "cudaGetDevice");
+  constexpr int kSmem = 150 * 1024;  // one CTA per SM
+  cudaError_t err = cudaFuncSetAttribute(probe_mma_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaFuncSetAttribute (probe)");
+  unsigned long long* clocks = nullptr;
+  if ((err = cudaMalloc(&clocks, sizeof(unsigned long long) * sms)) != cudaSuccess)
+    return cuda_fail(err, "cudaMalloc (probe)");
+  cudaEvent_t e0, e1;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  probe_mma_kernel<N><<<sms, 128, kSmem>>>(8, clocks);  // warm-up
+  cudaEventRecord(e0);
+  probe_mma_kernel<N><<<sms, 128, kSmem>>>(iters, clocks);
+  cudaEventRecord(e1);
+  err = cudaEventSynchronize(e1);
+  float ms = 0.f;
+  cudaEventElapsedTime(&ms, e0, e1);
+  std::vector<unsigned long long> h(sms);
+  if (err == cudaSuccess) err = cudaMemcpy(h.data(), clocks, sizeof(unsigned long long) * sms, cudaMemcpyDeviceToHost);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  cudaFree(clocks);
+  if (err != cudaSuccess) return cuda_fail(err, "probe launch");
+  std::sort(h.begin(), h.end());
+  const double macs = double(iters) * 4 * 128 * N * 32;  // per CTA
+  if (tflops) *tflops = 2.0 * macs * sms / (double(ms) * 1e-3) / 1e12;
+  if (macs_per_clock) *macs_per_clock = macs / double(h[h.size() / 2]);
+  return BFP8_OK;
+}
+
+}  // namespace
+
+extern "C" int bfp8_probe_mma(int n, int iters, double* tflops, double* macs_per_clock) {
+  if (iters <= 0) return fail(BFP8_EINVAL, "iters must be positive");
+  if (n == 256) return run_probe_mma<256>(iters, tflops, macs_per_clock);
+  if (n == 128) return run_probe_mma<128>(iters, tflops, macs_per_clock);
+  return fail(BFP8_EINVAL, "probe n must be 128 or 256");
+}
+
+extern "C" int bfp8_probe_hbm_read(const void* buf, int64_t bytes, int reps, double* gbs) {
+  if (!buf || bytes < 16 || reps <= 0 || !aligned16(buf)) return fail(BFP8_EINVAL, "probe buffer");
+  const int sms = current_device_sms(nullptr);
+  if (sms <= 0) return cuda_fail(cudaGetLastError(), "cudaGetDevice");
+  const int grid = sms * 8;
+  uint32_t* sink = nullptr;
+  cudaError_t err = cudaMalloc(&sink, sizeof(uint32_t) * grid * 256);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaMalloc (probe)");
+  const int64_t words = bytes / 16;
+  const uint4* p = static_cast<const uint4*>(buf);
+  cudaEvent_t e0, e1;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  bfp8::probe_read_kernel<<<grid, 256>>>(p, words, sink);  // warm-up
+  cudaEventRecord(e0);
+  for (int r = 0; r < reps; ++r) bfp8::probe_read_kernel<<<grid, 256>>>(p, words, sink);
+  cudaEventRecord(e1);
+  err = cudaEventSynchronize(e1);
+  float ms = 0.f;
+  cudaEventElapsedTime(&ms, e0, e1);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  cudaFree(sink);
+  if (err != cudaSuccess) return cuda_fail(err, "probe launch");
+  if (gbs) *gbs = double(words) * 16 * reps / (double(ms) * 1e-3) / 1e9;
+  return BFP8_OK;
+}

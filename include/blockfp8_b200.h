@@ -162,6 +162,15 @@ int64_t bfp8_device_status(int reset);
 /* ABI version of this header (1). */
 int bfp8_abi_version(void);
 
+/* Roofline probes.  No counterpart in the reference.  Measure, on the current
+ * device, the dense e4m3 tensor-core rate (back-to-back 128 x n x 32
+ * tcgen05 MMAs from shared memory on every SM, n = 128 or 256; TFLOP/s and
+ * multiply-adds per clock per SM) and the HBM read rate over a caller
+ * buffer of `bytes` (16-byte aligned, larger than L2), in GB/s.  They run
+ * synchronously and allocate a little scratch; not for the hot path. */
+int bfp8_probe_mma(int n, int iters, double* tflops, double* macs_per_clock);
+int bfp8_probe_hbm_read(const void* buf, int64_t bytes, int reps, double* gbs);
+
 #ifdef __cplusplus
 }
 #endif

@@ -137,3 +137,15 @@ def test_both_fused_modes_equal_the_quantized_gemm(m, n, k, splits):
     a_np, sa_np = oracle_quant(x.cpu())
     assert_close(expect, O.reference_gemm(a_np, sa_np, b_np, sb_np))
     assert _native.device_status(reset=True) == 0
+
+
+def test_roofline_probes_answer_in_range():
+    """The in-library probes: dense e4m3 MMA rate near the 8192 multiply-adds
+    per clock per SM of the tensor core, and an HBM read rate of several TB/s."""
+    tf, mpc = _native.probe_mma(256, 500)
+    assert 6000 < mpc <= 8200 and tf > 1500, (tf, mpc)
+    buf = torch.empty(2 << 30, dtype=torch.uint8, device=DEV)
+    gbs = _native.probe_hbm_read(buf, reps=3)
+    del buf
+    assert 3000 < gbs < 9000, gbs
+    assert _native.device_status(reset=True) == 0
