@@ -76,6 +76,7 @@ _SIGNATURES = {
                         ctypes.POINTER(ctypes.c_double)], ctypes.c_int),
     "bfp8_probe_hbm_read": ([ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.POINTER(ctypes.c_double)],
                             ctypes.c_int),
+    "bfp8_probe_block": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
 }
 
 _capi = None
@@ -164,3 +165,15 @@ def probe_hbm_read(buf, reps: int = 5) -> float:
     check(capi().bfp8_probe_hbm_read(ctypes.c_void_p(buf.data_ptr()), buf.numel() * buf.element_size(), reps,
                                      ctypes.byref(gbs)))
     return gbs.value
+
+
+def probe_block(a, b):
+    """fp32 [128, 32] raw tensor-core partial of e4m3 a [128, 128] @ b [32, 128]^T
+    (four K = 32 tcgen05 MMAs), on the current device."""
+    import torch
+    assert a.shape == (128, 128) and b.shape == (32, 128) and a.is_cuda and b.is_cuda
+    d = torch.empty(128, 32, dtype=torch.float32, device=a.device)
+    check(capi().bfp8_probe_block(ctypes.c_void_p(a.contiguous().data_ptr()),
+                                  ctypes.c_void_p(b.contiguous().data_ptr()), ctypes.c_void_p(d.data_ptr()),
+                                  ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+    return d

@@ -787,3 +787,14 @@ extern "C" int bfp8_probe_hbm_read(const void* buf, int64_t bytes, int reps, dou
   if (gbs) *gbs = double(words) * 16 * reps / (double(ms) * 1e-3) / 1e9;
   return BFP8_OK;
 }
+
+extern "C" int bfp8_probe_block(const void* a, const void* b, float* d, void* stream) {
+  if (!a || !b || !d || !aligned16(a) || !aligned16(b)) return fail(BFP8_EINVAL, "probe operands");
+  constexpr int kSmem = 1024 + 128 * 128 + 32 * 128;
+  cudaError_t err = cudaFuncSetAttribute(bfp8::probe_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaFuncSetAttribute (probe)");
+  bfp8::probe_block_kernel<<<1, 128, kSmem, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(a), static_cast<const uint8_t*>(b), d);
+  err = cudaGetLastError();
+  return err == cudaSuccess ? BFP8_OK : cuda_fail(err, "probe launch");
+}

@@ -60,6 +60,62 @@ __global__ void __launch_bounds__(128, 1) probe_mma_kernel(int iters, unsigned l
   }
 }
 
+// One 128 x 32 x 128 block product exactly as the GEMM forms a K block's
+// partial: A [128 x 128] and B [32 x 128] e4m3 (row-major, 128 bytes a row)
+// into 128-byte-swizzled shared memory, four K = 32 MMAs into TMEM (the
+// first with the accumulator input off), and the raw fp32 result
+// D [128 x 32] back to global memory.  For precision experiments.
+__global__ void __launch_bounds__(128, 1) probe_block_kernel(const uint8_t* __restrict__ a,
+                                                             const uint8_t* __restrict__ b, float* d) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  const uint32_t sb_tile = base + 128 * 128;
+  __shared__ uint64_t done;
+  __shared__ uint32_t slot;
+  const int warp = threadIdx.x >> 5, row = threadIdx.x;
+  // 16-byte unit u of row r sits at r * 128 + ((u ^ (r % 8)) * 16)
+  for (int u = 0; u < 8; ++u) {
+    const uint4 v = reinterpret_cast<const uint4*>(a + row * 128)[u];
+    st_shared_v4(base + uint32_t(row) * 128u + uint32_t((u ^ (row & 7)) * 16), v.x, v.y, v.z, v.w);
+    if (row < 32) {
+      const uint4 w = reinterpret_cast<const uint4*>(b + row * 128)[u];
+      st_shared_v4(sb_tile + uint32_t(row) * 128u + uint32_t((u ^ (row & 7)) * 16), w.x, w.y, w.z, w.w);
+    }
+  }
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&done), 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(smem_u32(&slot), 32);
+    tmem_relinquish();
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = slot;
+  if (threadIdx.x == 0) {
+    const uint64_t da = smem_desc_k128_sw128(base), db = smem_desc_k128_sw128(sb_tile);
+    constexpr uint32_t idesc = idesc_e4m3_f32(128, 32);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) mma_f8(tmem, da + 2 * k, db + 2 * k, idesc, k > 0 ? 1u : 0u);
+    mma_commit(smem_u32(&done));
+  }
+  mbar_wait(smem_u32(&done), 0, nullptr, kProbeWaitSite);
+  tc_fence_after();
+  float v[32];
+  tmem_ld32(tmem + (uint32_t(32 * warp) << 16), v);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) d[row * 32 + j] = v[j];
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 32);
+  }
+}
+
 // Reads every 16-byte word of buf once (grid-stride); one xor per thread goes
 // to sink so the loads are not dead.
 __global__ void __launch_bounds__(256) probe_read_kernel(const uint4* __restrict__ buf, int64_t words,

@@ -170,6 +170,11 @@ int bfp8_abi_version(void);
  * synchronously and allocate a little scratch; not for the hot path. */
 int bfp8_probe_mma(int n, int iters, double* tflops, double* macs_per_clock);
 int bfp8_probe_hbm_read(const void* buf, int64_t bytes, int reps, double* gbs);
+/* One K block's raw partial sums as the GEMM's tensor cores form them:
+ * a [128 x 128] and b [32 x 128] e4m3 row-major device arrays (16-byte
+ * aligned) -> d [128 x 32] fp32 = four K = 32 tcgen05 MMAs, unscaled, before
+ * any rounding of the GEMM's own.  For measuring the MMA's accumulation. */
+int bfp8_probe_block(const void* a, const void* b, float* d, void* stream);
 
 #ifdef __cplusplus
 }
