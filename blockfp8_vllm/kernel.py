@@ -31,6 +31,13 @@ def block_scale_of(params) -> torch.Tensor:
 class BlockFp8LinearKernel(Fp8BlockScaledMMLinearKernel):
     """W8A8 block-FP8 linear on B200: blockfp8.linear on checkpoint weights."""
 
+    def __init__(self, config) -> None:
+        super().__init__(config)
+        # torch.ops.blockfp8.* exist once _C.so is loaded; vLLM may build a
+        # kernel without asking is_supported() first (force_kernel)
+        if not blockfp8.native_available():
+            raise RuntimeError("BlockFp8LinearKernel needs the built blockfp8_b200 native libraries")
+
     @classmethod
     def is_supported(cls, compute_capability: int | None = None) -> tuple[bool, str | None]:
         if not current_platform.is_cuda():
