@@ -52,6 +52,21 @@ class QuantProblem(ctypes.Structure):
     ]
 
 
+TP_MAX_RANKS = 8
+IPC_HANDLE_BYTES = 64
+
+
+class TpGroup(ctypes.Structure):
+    """bfp8_tp_group: a row-parallel group as one launch sees it."""
+    _fields_ = [
+        ("world", ctypes.c_int), ("rank", ctypes.c_int), ("wait", ctypes.c_int),
+        ("done_target", ctypes.c_ulonglong),
+        ("partials", ctypes.c_void_p * TP_MAX_RANKS),
+        ("counters", ctypes.c_void_p * TP_MAX_RANKS),
+        ("out", ctypes.c_void_p * TP_MAX_RANKS),
+    ]
+
+
 # Every function the header declares, with its ctypes signature.
 _SIGNATURES = {
     "bfp8_abi_version": ([], ctypes.c_int),
@@ -70,6 +85,14 @@ _SIGNATURES = {
     "bfp8_launch_gemm": ([ctypes.POINTER(GemmProblem), Plan, ctypes.c_void_p, ctypes.c_void_p,
                           ctypes.c_void_p], ctypes.c_int),
     "bfp8_launch_gemm_noalloc": ([ctypes.POINTER(GemmProblem), Plan, ctypes.c_void_p], ctypes.c_int),
+    "bfp8_tp_tiles": ([ctypes.POINTER(GemmProblem), Plan], ctypes.c_int),
+    "bfp8_tp_partial_bytes": ([ctypes.POINTER(GemmProblem), Plan, ctypes.c_int], ctypes.c_int64),
+    "bfp8_launch_gemm_tp": ([ctypes.POINTER(GemmProblem), Plan, ctypes.c_void_p, ctypes.c_void_p,
+                             ctypes.POINTER(TpGroup), ctypes.c_void_p], ctypes.c_int),
+    "bfp8_tp_alloc": ([ctypes.c_int64, ctypes.POINTER(ctypes.c_void_p), ctypes.c_char_p], ctypes.c_int),
+    "bfp8_tp_open": ([ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
+    "bfp8_tp_close": ([ctypes.c_void_p], ctypes.c_int),
+    "bfp8_tp_free": ([ctypes.c_void_p], ctypes.c_int),
     "bfp8_launch_quantize": ([ctypes.POINTER(QuantProblem), ctypes.c_void_p], ctypes.c_int),
     "bfp8_device_status": ([ctypes.c_int], ctypes.c_int64),
     "bfp8_probe_mma": ([ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_double),

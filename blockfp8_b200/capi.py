@@ -91,3 +91,23 @@ def quantize(x: torch.Tensor, eps: float = 1e-10, stream=None):
     p.M, p.K, p.eps = m, k, eps
     check(_native.capi().bfp8_launch_quantize(ctypes.byref(p), _stream(stream)))
     return q, s
+
+
+def launch_gemm_tp(p: GemmProblem, plan: Plan, tp: _native.TpGroup, workspace=None, counters=None,
+                   stream=None) -> None:
+    """bfp8_launch_gemm_tp: the GEMM of one rank of a row-parallel group, its
+    all-reduce included (tp describes the group's buffers)."""
+    check(_native.capi().bfp8_launch_gemm_tp(ctypes.byref(p), plan, _ptr(workspace), _ptr(counters),
+                                             ctypes.byref(tp), _stream(stream)))
+
+
+def tp_tiles(p: GemmProblem, plan: Plan) -> int:
+    n = _native.capi().bfp8_tp_tiles(ctypes.byref(p), plan)
+    check(n if n < 0 else 0)
+    return n
+
+
+def tp_partial_bytes(p: GemmProblem, plan: Plan, world: int) -> int:
+    n = _native.capi().bfp8_tp_partial_bytes(ctypes.byref(p), plan, world)
+    check(n if n < 0 else 0)
+    return n

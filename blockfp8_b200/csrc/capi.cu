@@ -59,6 +59,11 @@ struct ConfigEntry {
   const void* kernel_fused = nullptr;
   void (*launch_fused)(const GemmParams&, int grid, cudaStream_t) = nullptr;
   int smem_fused = 0, threads_fused = 0;
+  // The row-parallel twins (bfp8_launch_gemm_tp) of both kernels.
+  const void* kernel_tp = nullptr;
+  void (*launch_tp)(const GemmParams&, int grid, cudaStream_t) = nullptr;
+  const void* kernel_fused_tp = nullptr;
+  void (*launch_fused_tp)(const GemmParams&, int grid, cudaStream_t) = nullptr;
   int act_kb = 0;  // K blocks of one unit the in-kernel variant keeps resident
 };
 
@@ -88,8 +93,11 @@ void launch_cfg(const GemmParams& gp, int grid, cudaStream_t stream) {
 
 template <class Cfg>
 ConfigEntry entry(const char* name) {
-  return {name, Cfg::BN, Cfg::STAGES, Cfg::THREADS, Cfg::SMEM_BYTES, Cfg::SWAP, Cfg::TILE_M, Cfg::PAIR,
-          reinterpret_cast<const void*>(&gemm_kernel<Cfg>), &launch_cfg<Cfg>};
+  ConfigEntry e{name, Cfg::BN, Cfg::STAGES, Cfg::THREADS, Cfg::SMEM_BYTES, Cfg::SWAP, Cfg::TILE_M, Cfg::PAIR,
+                reinterpret_cast<const void*>(&gemm_kernel<Cfg>), &launch_cfg<Cfg>};
+  e.kernel_tp = reinterpret_cast<const void*>(&gemm_kernel<WithTp<Cfg>>);
+  e.launch_tp = &launch_cfg<WithTp<Cfg>>;
+  return e;
 }
 
 template <class Cfg, class FusedCfg>
@@ -99,6 +107,8 @@ ConfigEntry entry_fused(const char* name) {
   e.launch_fused = &launch_cfg<FusedCfg>;
   e.smem_fused = FusedCfg::SMEM_BYTES;
   e.threads_fused = FusedCfg::THREADS;
+  e.kernel_fused_tp = reinterpret_cast<const void*>(&gemm_kernel<WithTp<FusedCfg>>);
+  e.launch_fused_tp = &launch_cfg<WithTp<FusedCfg>>;
   e.act_kb = FusedCfg::ACT_KB;
   return e;
 }
@@ -161,14 +171,14 @@ int current_device_sms(int* dev_out) {
 
 // The dynamic shared-memory limit is a per-device attribute of a kernel:
 // set it on the first launch of each configuration on each device.
-int ensure_smem_attr(int config, int dev, bool in_kernel_quant) {
-  static std::atomic<uint64_t> done[2][kNumConfigs] = {};
+int ensure_smem_attr(int config, int dev, bool in_kernel_quant, bool tp = false) {
+  static std::atomic<uint64_t> done[4][kNumConfigs] = {};
   const uint64_t bit = dev < 64 ? (uint64_t(1) << dev) : 0;
-  std::atomic<uint64_t>& d = done[in_kernel_quant ? 1 : 0][config];
+  std::atomic<uint64_t>& d = done[(in_kernel_quant ? 1 : 0) + (tp ? 2 : 0)][config];
   if (bit && (d.load(std::memory_order_acquire) & bit)) return BFP8_OK;
   const ConfigEntry& e = kConfigs[config];
-  cudaError_t err = cudaFuncSetAttribute(in_kernel_quant ? e.kernel_fused : e.kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+  const void* kernel = in_kernel_quant ? (tp ? e.kernel_fused_tp : e.kernel_fused) : (tp ? e.kernel_tp : e.kernel);
+  cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          in_kernel_quant ? e.smem_fused : e.smem);
   if (err != cudaSuccess) return cuda_fail(err, "cudaFuncSetAttribute(MaxDynamicSharedMemorySize)");
   d.fetch_or(bit, std::memory_order_release);
@@ -558,8 +568,25 @@ int bfp8_launch_quantize(const bfp8_quant_problem* qp, void* stream) {
   return launch_quant(q, static_cast<cudaStream_t>(stream), sms);
 }
 
-int bfp8_launch_gemm(const bfp8_gemm_problem* pp, bfp8_plan plan, float* workspace, int* counters,
-                     void* stream_) {
+namespace bfp8 {
+namespace {
+
+// Checks a row-parallel group against the problem (every pointer the kernel
+// will use, this rank's output = p.c).
+int check_tp(const bfp8_gemm_problem& p, const bfp8_tp_group& tp) {
+  if (tp.world < 1 || tp.world > BFP8_TP_MAX_RANKS) return fail(BFP8_EINVAL, "tp world must be 1..8");
+  if (tp.rank < 0 || tp.rank >= tp.world) return fail(BFP8_EINVAL, "tp rank out of range");
+  for (int q = 0; q < tp.world; ++q) {
+    if (!tp.partials[q] || !tp.counters[q] || !tp.out[q]) return fail(BFP8_EINVAL, "null tp buffer");
+    if (!aligned16(tp.partials[q]) || !aligned16(tp.out[q]) || (reinterpret_cast<uintptr_t>(tp.counters[q]) & 7u))
+      return fail(BFP8_EINVAL, "tp buffers must be 16-byte aligned (counters 8-byte)");
+  }
+  if (tp.out[tp.rank] != p.c) return fail(BFP8_EINVAL, "c must be this rank's tp output (out[rank])");
+  return BFP8_OK;
+}
+
+int launch_gemm_impl(const bfp8_gemm_problem* pp, bfp8_plan plan, float* workspace, int* counters,
+                     const bfp8_tp_group* tp, void* stream_) {
   if (!pp) return fail(BFP8_EINVAL, "null problem");
   if (!config_ok(plan.config)) return fail(BFP8_EINVAL, "config out of range");
   if (plan.splits == 0) return fail(BFP8_EINVAL, "splits must be >= 1 (or negative: stream-K)");
@@ -657,14 +684,99 @@ int bfp8_launch_gemm(const bfp8_gemm_problem* pp, bfp8_plan plan, float* workspa
   gp.group_r = e.swap || a_bytes <= (int64_t(48) << 20) ? d.tiles_r : 1024 / e.bm;
   gp.stream_b = (e.swap || p.M <= 128) ? 1 : 0;  // weights read once: evict them first
   gp.pdl = fused && !in_kernel ? 1 : 0;
+  if (tp) {
+    gp.tp_world = tp->world;
+    gp.tp_rank = tp->rank;
+    gp.tp_wait = tp->wait ? 1 : 0;
+    gp.tp_done_target = tp->done_target;
+    for (int q = 0; q < tp->world; ++q) {
+      gp.tp_partials[q] = tp->partials[q];
+      gp.tp_counters[q] = tp->counters[q];
+      gp.tp_out[q] = static_cast<__nv_bfloat16*>(tp->out[q]);
+    }
+    gp.tp_ldo = p.ldc;
+  }
 
-  if (int r = ensure_smem_attr(plan.config, dev, in_kernel)) return r;
+  if (int r = ensure_smem_attr(plan.config, dev, in_kernel, tp != nullptr)) return r;
   // One CTA (a pair: two) per SM, persistent over the units.
   const int grid = d.sk_grid > 0 ? d.sk_grid : e.pair ? 2 * std::min(gp.units, sms / 2) : std::min(gp.units, sms);
-  (in_kernel ? e.launch_fused : e.launch)(gp, grid, stream);
+  (in_kernel ? (tp ? e.launch_fused_tp : e.launch_fused) : (tp ? e.launch_tp : e.launch))(gp, grid, stream);
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return cuda_fail(err, "GEMM kernel launch");
   return BFP8_OK;
+}
+
+}  // namespace
+}  // namespace bfp8
+
+int bfp8_launch_gemm(const bfp8_gemm_problem* p, bfp8_plan plan, float* workspace, int* counters, void* stream) {
+  return launch_gemm_impl(p, plan, workspace, counters, nullptr, stream);
+}
+
+int bfp8_tp_tiles(const bfp8_gemm_problem* p, bfp8_plan plan) {
+  if (!p || !config_ok(plan.config)) return fail(BFP8_EINVAL, "bad config id");
+  if (int r = check_schedule(plan)) return r;
+  if (p->M <= 0) return 0;
+  const Derived d = derive(*p, plan);
+  return d.tiles * (kConfigs[plan.config].bm / 128);
+}
+
+int64_t bfp8_tp_partial_bytes(const bfp8_gemm_problem* p, bfp8_plan plan, int world) {
+  if (world < 1 || world > BFP8_TP_MAX_RANKS) return fail(BFP8_EINVAL, "tp world must be 1..8");
+  const int tiles = bfp8_tp_tiles(p, plan);
+  if (tiles < 0) return tiles;
+  return int64_t(world) * tiles * 128 * kConfigs[plan.config].bn * int64_t(sizeof(float));
+}
+
+int bfp8_launch_gemm_tp(const bfp8_gemm_problem* p, bfp8_plan plan, float* workspace, int* counters,
+                        const bfp8_tp_group* tp, void* stream) {
+  if (!p || !tp) return fail(BFP8_EINVAL, "null problem or tp group");
+  if (!config_ok(plan.config)) return fail(BFP8_EINVAL, "config out of range");
+  if (p->M > 0)
+    if (int r = check_tp(*p, *tp)) return r;
+  return launch_gemm_impl(p, plan, workspace, counters, tp, stream);
+}
+
+static_assert(sizeof(cudaIpcMemHandle_t) == BFP8_IPC_HANDLE_BYTES, "CUDA IPC handle size");
+
+int bfp8_tp_alloc(int64_t bytes, void** ptr, void* handle) {
+  if (!ptr || !handle || bytes <= 0) return fail(BFP8_EINVAL, "tp alloc: null output or non-positive size");
+  *ptr = nullptr;
+  void* d = nullptr;
+  cudaError_t e = cudaMalloc(&d, size_t(bytes));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(tp buffer)");
+  e = cudaMemset(d, 0, size_t(bytes));
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, d);
+  if (e != cudaSuccess) {
+    cudaFree(d);
+    return cuda_fail(e, "tp buffer set-up");
+  }
+  std::memcpy(handle, &h, sizeof(h));
+  *ptr = d;
+  return BFP8_OK;
+}
+
+int bfp8_tp_open(const void* handle, void** ptr) {
+  if (!handle || !ptr) return fail(BFP8_EINVAL, "tp open: null argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  *ptr = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+  return BFP8_OK;
+}
+
+int bfp8_tp_close(void* ptr) {
+  if (!ptr) return BFP8_OK;
+  cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  return e == cudaSuccess ? BFP8_OK : cuda_fail(e, "cudaIpcCloseMemHandle");
+}
+
+int bfp8_tp_free(void* ptr) {
+  if (!ptr) return BFP8_OK;
+  cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? BFP8_OK : cuda_fail(e, "cudaFree(tp buffer)");
 }
 
 int bfp8_launch_gemm_noalloc(const bfp8_gemm_problem* p, bfp8_plan plan, void* stream) {

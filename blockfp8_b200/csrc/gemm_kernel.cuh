@@ -74,6 +74,8 @@
 
 namespace bfp8 {
 
+constexpr int kTpMaxRanks = 8;  // ranks of a row-parallel group
+
 struct GemmParams {
   CUtensorMap map_a;  // MMA A operand (128-row tiles): activations, or weights when swapped
   CUtensorMap map_b;  // MMA B operand (BN-row tiles): weights, or activations when swapped
@@ -96,11 +98,27 @@ struct GemmParams {
   const __nv_bfloat16* x;  // in-kernel quantization: bf16 activations [M, K], row stride ldx
   int64_t ldx;
   float eps;  // in-kernel quantization: floor of each group's amax
+  // Row-parallel reduction (tp_world >= 1; 0 = off): every rank of a group
+  // computes the same [M, N] over its own K slice.  Tile t's fp32 sum from
+  // rank r goes to slot [r][t] of rank (t % world)'s tp_partials; the rank
+  // whose arrival on that rank's counter [1 + t] completes the count sums
+  // the slots in rank order, stores bf16 into every rank's tp_out and adds
+  // one to every rank's counter [0].  With tp_wait, CTA 0 waits (bounded)
+  // until its own counter [0] reaches tp_done_target.
+  int tp_world, tp_rank, tp_wait;
+  unsigned long long tp_done_target;
+  float* tp_partials[kTpMaxRanks];               // [world][tiles][128 * BN] fp32, per rank
+  unsigned long long* tp_counters[kTpMaxRanks];  // [0]: tiles delivered, [1 + t]: arrivals on tile t
+  __nv_bfloat16* tp_out[kTpMaxRanks];            // bf16 [M, N], row stride tp_ldo, per rank
+  int64_t tp_ldo;
 };
 
-template <int BN_, int STAGES_, bool SWAP_, bool FUSE_ = false, bool PAIR_ = false>
+template <int BN_, int STAGES_, bool SWAP_, bool FUSE_ = false, bool PAIR_ = false, bool TP_ = false>
 struct GemmCfg {
   static constexpr int BM = 128, BN = BN_, BK = 128, STAGES = STAGES_;
+  // TP: the row-parallel twin of a configuration: a tile's sum goes into
+  // the group's reduction (GemmParams tp_*) instead of a bf16 store.
+  static constexpr bool TP = TP_;
   static constexpr bool SWAP = SWAP_;
   static constexpr bool FUSE = FUSE_;
   // PAIR: a cluster of two CTAs on a 256 x BN tile with cta_group::2 MMAs
@@ -172,6 +190,10 @@ struct GemmCfg {
   static_assert(STAGE_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "tiles must stay 1024-byte aligned");
 };
 
+// The row-parallel twin of configuration C.
+template <class C>
+using WithTp = GemmCfg<C::BN, C::STAGES, C::SWAP, C::FUSE, C::PAIR, true>;
+
 enum WaitSite : uint32_t {
   kWaitEmpty = 1,
   kWaitFull = 2,
@@ -180,6 +202,7 @@ enum WaitSite : uint32_t {
   kWaitDrain = 5,
   kWaitMmaDone = 6,
   kWaitActReady = 7,  // a resident activation K block (FUSE)
+  kWaitTpDelivered = 8,  // row-parallel: the other ranks' tiles of this rank's output
 };
 
 // A unit: one tile's K blocks kt0 .. kt1 - 1, the part `split` of the tile's
@@ -684,6 +707,74 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
       publish_unit(c_next, 0);
     }
 
+    // Row-parallel hand-off of a tile this CTA holds whole (every epilogue
+    // thread calls it; the barriers inside are CTA-wide).  The partial goes
+    // in [column][row] order so a warp's stores and loads cover 128
+    // contiguous bytes, local or across NVLink.  No CTA waits here: the
+    // last of the world arrivals does the sum.
+    auto tp_reduce = [&](const UnitCoord& c, int r, bool row_ok, bool cols_ok, int col0, float (&accum)[COLS],
+                         bool ok) {
+      const int W = p.tp_world;
+      const int wtile = PAIR ? c.tile * 2 + int(rank) : c.tile;
+      const int64_t wtiles = int64_t(p.tiles) * (PAIR ? 2 : 1);
+      const int owner = wtile % W;
+      const int64_t rank_stride = wtiles * (128 * BN);
+      // Column j of this thread's accumulators is tile column cidx(j).
+      auto cidx = [&](int j) { return SWAP ? j : g * COLS + j; };
+      float* slots = p.tp_partials[owner] + int64_t(wtile) * (128 * BN) + row;
+      if (row_ok && cols_ok && ok) {
+        float* w = slots + p.tp_rank * rank_stride;
+#pragma unroll
+        for (int j = 0; j < COLS; ++j) __stcg(w + cidx(j) * 128, accum[j]);
+      }
+      named_bar_sync(1, Cfg::EPI_THREADS);
+      if (ew == 0 && lane == 0) {
+        fence_acq_rel_sys();  // every thread's partial (ordered by the barrier) before the count
+        unsigned long long* cnt = p.tp_counters[owner] + 1 + wtile;
+        const bool last = atom_add_acq_rel_sys(cnt, 1ull) == static_cast<unsigned long long>(W - 1);
+        // Reset for the next call: no rank counts on this tile again before
+        // it has seen this tile delivered (its kernel waits for that).
+        if (last) st_relaxed_sys(cnt, 0ull);
+        *last_flag = last;
+      }
+      named_bar_sync(1, Cfg::EPI_THREADS);
+      if (*last_flag == 0) return;
+      if (row_ok && cols_ok && ok) {
+        // Sum the ranks' partials in rank order from zero, round once to bf16.
+#pragma unroll
+        for (int j = 0; j < COLS; ++j) accum[j] = 0.f;
+        for (int s = 0; s < W; ++s) {
+          const float* w = slots + s * rank_stride;
+#pragma unroll
+          for (int j = 0; j < COLS; ++j) accum[j] += __ldcg(w + cidx(j) * 128);
+        }
+        for (int q = 0; q < W; ++q) {
+          if constexpr (!SWAP) {
+            // Row r, columns col0 .. col0 + COLS - 1 in 16-byte pieces (N and
+            // the row stride are multiples of 8, outputs 16-byte aligned).
+            __nv_bfloat16* o = p.tp_out[q] + int64_t(r) * p.tp_ldo + col0;
+#pragma unroll
+            for (int j = 0; j < COLS; j += 8)
+              if (col0 + j < p.N)
+                *reinterpret_cast<uint4*>(o + j) = make_uint4(
+                    bf16x2_bits(accum[j], accum[j + 1]), bf16x2_bits(accum[j + 2], accum[j + 3]),
+                    bf16x2_bits(accum[j + 4], accum[j + 5]), bf16x2_bits(accum[j + 6], accum[j + 7]));
+          } else {
+            // Weight row r is output column r; token col0 + j is output row.
+            __nv_bfloat16* o = p.tp_out[q] + r;
+#pragma unroll
+            for (int j = 0; j < COLS; ++j)
+              if (col0 + j < p.M) o[int64_t(col0 + j) * p.tp_ldo] = __float2bfloat16_rn(accum[j]);
+          }
+        }
+      }
+      named_bar_sync(1, Cfg::EPI_THREADS);
+      if (ew == 0 && lane == 0) {
+        fence_acq_rel_sys();  // the tile's outputs before the delivery counts
+        for (int q = 0; q < W; ++q) red_add_release_sys(p.tp_counters[q], 1ull);
+      }
+    };
+
     int next_seq = 0;  // position of the next unit's first K block in the CTA's sequence
     for (int u = u0; any_unit && unit_valid(p, u, sid);) {
       const UnitCoord c = c_next;
@@ -808,6 +899,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
       }
 
       bool store = work;
+      bool tile_whole = true;  // this CTA holds the tile's sum over its K range
       if (c.pieces > 1) {
         // Deterministic split-K: publish this split's partial, count arrivals;
         // the last CTA of the tile sums all partials in split order.
@@ -837,6 +929,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
         named_bar_sync(1, Cfg::EPI_THREADS);
         const bool last = *last_flag != 0;
         store = store && last;
+        tile_whole = last;
         if (last) {
           if (row_ok && cols_ok) {
             // Sum every split's partial (this CTA's own included, as written
@@ -866,7 +959,9 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
         }
       }
 
-      if (store && ok) {
+      if constexpr (Cfg::TP) {
+        if (tile_whole) tp_reduce(c, r, row_ok, cols_ok, col0, accum, ok);  // CTA-uniform
+      } else if (store && ok) {
         if constexpr (!SWAP) {
           // bf16 rows -> [32 x 32] chunks, 64-byte swizzle, two buffers in
           // turn so one chunk's TMA store overlaps the next chunk's writes.
@@ -907,6 +1002,19 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
             bulk_commit();
           }
         }
+      }
+    }
+    if (Cfg::TP && p.tp_wait && blockIdx.x == 0 && ew == 0 && lane == 0) {
+      // This rank's output is complete once every tile has been delivered
+      // (by whichever rank summed it); the kernel ends after that.
+      const uint64_t t0 = globaltimer();
+      while (ld_acquire_sys(p.tp_counters[p.tp_rank]) < p.tp_done_target) {
+        if (*abort_flag || globaltimer() - t0 > kWaitTimeoutNs) {
+          record_status((0x5Bull << 56) | (uint64_t(kWaitTpDelivered) << 32) | (uint64_t(blockIdx.x) << 8) |
+                        uint64_t(warp));
+          break;
+        }
+        __nanosleep(64);
       }
     }
     if (lane == 0) bulk_wait0();  // stores complete before the CTA retires

@@ -211,6 +211,27 @@ __device__ __forceinline__ int atom_add_acq_rel_gpu(int* ptr, int v) {
   return old;
 }
 
+// System-scope versions for the row-parallel reduction, whose partial sums,
+// counters and outputs live in other GPUs' memory (NVLink peer mappings).
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ unsigned long long atom_add_acq_rel_sys(unsigned long long* ptr,
+                                                                   unsigned long long v) {
+  unsigned long long old;
+  asm volatile("atom.acq_rel.sys.global.add.u64 %0, [%1], %2;" : "=l"(old) : "l"(ptr), "l"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ void red_add_release_sys(unsigned long long* ptr, unsigned long long v) {
+  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(ptr), "l"(v) : "memory");
+}
+__device__ __forceinline__ void st_relaxed_sys(unsigned long long* ptr, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(ptr), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* ptr) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(ptr) : "memory");
+  return v;
+}
+
 // ---- named barriers (a subset of the CTA's warps) ---------------------------------
 
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {

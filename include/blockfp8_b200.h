@@ -145,6 +145,62 @@ int bfp8_launch_gemm(const bfp8_gemm_problem* p, bfp8_plan plan, float* workspac
 #define BFP8_STATIC_COUNTER_BYTES (64u << 10)
 int bfp8_launch_gemm_noalloc(const bfp8_gemm_problem* p, bfp8_plan plan, void* stream);
 
+/* ---- row-parallel linear with its all-reduce inside the GEMM ------------------
+ * Replaces the GEMM + NCCL all-reduce of a row-parallel (K-split) layer --
+ * the o and down projections of a tensor-parallel model, where vLLM's
+ * RowParallelLinear calls the block-FP8 GEMM (blockfp8_vllm/kernel.py:42-61)
+ * and then all-reduces the bf16 outputs.  Every rank of a group of `world`
+ * GPUs launches the same problem shape and plan over its own K slice.  Each
+ * tile's fp32 sum goes to one rank's partial buffer over NVLink (peer
+ * stores); the rank that completes a tile's count sums the `world` partials
+ * in rank order from zero, rounds once to bf16 and stores the tile into
+ * every rank's output; so the result is the same on every rank and from
+ * call to call.  No CTA waits for another rank inside the tile loop; with
+ * wait = 1 one thread waits (bounded, about 2 s, then the device status
+ * records site 8) at the end until this rank's output is complete.
+ *
+ * Buffers, per rank, mapped into every other rank (bfp8_tp_alloc /
+ * bfp8_tp_open):
+ *   partials: bfp8_tp_partial_bytes() (with this world size) bytes;
+ *   counters: 1 + bfp8_tp_tiles() unsigned 64-bit, zero at allocation:
+ *             [0] counts tiles delivered to this rank (never reset), [1 + t]
+ *             arrivals on tile t (the kernel resets them);
+ *   out:      the bf16 output [M, N] (row stride p->ldc, the same on every
+ *             rank); p->c must be out[rank].
+ * done_target: the value counters[0] of this rank reaches when this call's
+ * tiles are in: the sum of bfp8_tp_tiles() over the group's calls so far,
+ * this one included (the same on every rank).  All ranks make the same
+ * calls in the same order; a call's output stays valid until the group's
+ * next call.  After an error (a bounded wait gave up) the group's counters
+ * are no longer consistent: make a new group.  wait = 0 leaves the ordering
+ * to the caller (e.g. ranks emulated one after another on one GPU).
+ * No counterpart in the reference. */
+#define BFP8_TP_MAX_RANKS 8
+typedef struct bfp8_tp_group {
+  int world, rank;
+  int wait;
+  unsigned long long done_target;
+  float* partials[BFP8_TP_MAX_RANKS];
+  unsigned long long* counters[BFP8_TP_MAX_RANKS];
+  void* out[BFP8_TP_MAX_RANKS];
+} bfp8_tp_group;
+
+int bfp8_tp_tiles(const bfp8_gemm_problem* p, bfp8_plan plan);
+int64_t bfp8_tp_partial_bytes(const bfp8_gemm_problem* p, bfp8_plan plan, int world);
+int bfp8_launch_gemm_tp(const bfp8_gemm_problem* p, bfp8_plan plan, float* workspace, int* counters,
+                        const bfp8_tp_group* tp, void* stream);
+
+/* Peer buffers for a group: bfp8_tp_alloc cudaMallocs `bytes` (zeroed) on
+ * the current device and writes its CUDA IPC handle (64 bytes) to `handle`;
+ * another rank's process maps it with bfp8_tp_open (peer access enabled on
+ * first use) and unmaps it with bfp8_tp_close; the owner frees it with
+ * bfp8_tp_free.  No counterpart in the reference. */
+#define BFP8_IPC_HANDLE_BYTES 64
+int bfp8_tp_alloc(int64_t bytes, void** ptr, void* handle);
+int bfp8_tp_open(const void* handle, void** ptr);
+int bfp8_tp_close(void* ptr);
+int bfp8_tp_free(void* ptr);
+
 /* Launch the activation quantizer; replaces launch_quantize
  * (csrc/blockfp8.h:76).  Returns BFP8_OK, BFP8_EINVAL or BFP8_ECUDA. */
 int bfp8_launch_quantize(const bfp8_quant_problem* p, void* stream);

@@ -266,3 +266,41 @@ def test_row_parallel_linear_resolves_the_linear_function():
     assert callable(gemm_attr) and not inspect.ismodule(gemm_attr)
     src = inspect.getsource(sharding.row_parallel_linear)
     assert "from .gemm import linear" in src and callable(linear)
+
+
+def test_row_parallel_sizes_and_argument_checks():
+    """bfp8_tp_tiles / bfp8_tp_partial_bytes follow the tile grid (a CTA
+    pair's tile counts twice); bfp8_launch_gemm_tp rejects bad groups before
+    touching a device."""
+    lib = _native.capi()
+    names = [lib.bfp8_config_name(i).decode() for i in range(lib.bfp8_num_configs())]
+    for m, n in [(1, 4096), (300, 520), (8192, 24576)]:
+        p = _native.GemmProblem(M=m, N=n, K=2048)
+        for config, name in enumerate(names):
+            bm, bn = (int(v) for v in re.match(r"[mw](\d+)[nt](\d+)", name).groups())
+            rows, cols = (n, m) if name.startswith("w") else (m, n)
+            tiles = -(-rows // bm) * -(-cols // bn) * (bm // 128)
+            plan = _native.Plan(config, 1, 0)
+            assert lib.bfp8_tp_tiles(ctypes.byref(p), plan) == tiles
+            for world in (1, 2, 8):
+                assert lib.bfp8_tp_partial_bytes(ctypes.byref(p), plan, world) == world * tiles * 128 * bn * 4
+            assert lib.bfp8_tp_partial_bytes(ctypes.byref(p), plan, 9) < 0
+    p = _native.GemmProblem(a=256, lda=512, b=512, ldb=512, sa=1024, sa_m=1, sa_k=16, sb=2048, sb_n=4, sb_k=1,
+                            c=4096, ldc=256, M=16, N=256, K=512)
+    plan = _native.Plan(0, 1, 0)
+
+    def launch(**kw):
+        tp = _native.TpGroup(world=kw.get("world", 2), rank=kw.get("rank", 1), wait=0, done_target=1)
+        for q in range(8):
+            tp.partials[q], tp.counters[q], tp.out[q] = 8192, 16384, 4096 + 65536 * q
+        tp.out[1] = kw.get("own", 4096)
+        rc = lib.bfp8_launch_gemm_tp(ctypes.byref(p), plan, None, None, ctypes.byref(tp), None)
+        return rc, lib.bfp8_last_error().decode()
+
+    assert launch(world=0)[0] == _native.BFP8_EINVAL and "1..8" in launch(world=0)[1]
+    assert launch(world=9)[0] == _native.BFP8_EINVAL
+    assert "rank" in launch(rank=2)[1]
+    assert "out[rank]" in launch(own=8192)[1]
+    assert "aligned" in launch(own=4100)[1]
+    rc, msg = launch()  # a valid group: the first CUDA call fails here (no device)
+    assert rc == _native.BFP8_ECUDA, msg
