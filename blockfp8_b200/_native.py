@@ -60,7 +60,6 @@ class TpGroup(ctypes.Structure):
     """bfp8_tp_group: a row-parallel group as one launch sees it."""
     _fields_ = [
         ("world", ctypes.c_int), ("rank", ctypes.c_int), ("wait", ctypes.c_int),
-        ("done_target", ctypes.c_ulonglong),
         ("partials", ctypes.c_void_p * TP_MAX_RANKS),
         ("counters", ctypes.c_void_p * TP_MAX_RANKS),
         ("out", ctypes.c_void_p * TP_MAX_RANKS),

@@ -688,7 +688,11 @@ int launch_gemm_impl(const bfp8_gemm_problem* pp, bfp8_plan plan, float* workspa
     gp.tp_world = tp->world;
     gp.tp_rank = tp->rank;
     gp.tp_wait = tp->wait ? 1 : 0;
-    gp.tp_done_target = tp->done_target;
+    // Rank r starts at the first tile of rank r + 1's block (tile t belongs
+    // to rank floor(t * world / tiles), so block q starts at
+    // ceil(q * tiles / world)) and reaches its own block last.
+    const int64_t next = (tp->rank + 1) % tp->world;
+    gp.tp_rot = int((next * d.tiles + tp->world - 1) / tp->world) % d.tiles;
     for (int q = 0; q < tp->world; ++q) {
       gp.tp_partials[q] = tp->partials[q];
       gp.tp_counters[q] = tp->counters[q];

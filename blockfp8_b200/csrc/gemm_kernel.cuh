@@ -98,17 +98,19 @@ struct GemmParams {
   const __nv_bfloat16* x;  // in-kernel quantization: bf16 activations [M, K], row stride ldx
   int64_t ldx;
   float eps;  // in-kernel quantization: floor of each group's amax
-  // Row-parallel reduction (tp_world >= 1; 0 = off): every rank of a group
-  // computes the same [M, N] over its own K slice.  Tile t's fp32 sum from
-  // rank r goes to slot [r][t] of rank (t % world)'s tp_partials; the rank
-  // whose arrival on that rank's counter [1 + t] completes the count sums
-  // the slots in rank order, stores bf16 into every rank's tp_out and adds
-  // one to every rank's counter [0].  With tp_wait, CTA 0 waits (bounded)
-  // until its own counter [0] reaches tp_done_target.
-  int tp_world, tp_rank, tp_wait;
-  unsigned long long tp_done_target;
-  float* tp_partials[kTpMaxRanks];               // [world][tiles][128 * BN] fp32, per rank
-  unsigned long long* tp_counters[kTpMaxRanks];  // [0]: tiles delivered, [1 + t]: arrivals on tile t
+  // Row-parallel reduction (TP configurations): every rank of a group
+  // computes the same [M, N] over its own K slice.  Tile t belongs to rank
+  // floor(t * world / tiles) (contiguous blocks); rank r's schedule is
+  // rotated by tp_rot so it reaches its own block last.  Tile half w's
+  // fp32 sum from rank r goes to slot [r][w] of the owner's tp_partials;
+  // the arrival that completes the owner's count [2 + w] (usually the
+  // owner's own) sums the slots in rank order, stores bf16 into every
+  // rank's tp_out and adds one to every rank's counter [0].  At the end CTA
+  // 0 advances its rank's counter [1] by this call's tile halves, waiting
+  // first (bounded, with tp_wait) until counter [0] has caught up.
+  int tp_world, tp_rank, tp_wait, tp_rot;
+  float* tp_partials[kTpMaxRanks];               // [world][tile halves][128 * BN] fp32, per rank
+  unsigned long long* tp_counters[kTpMaxRanks];  // [0] delivered, [1] consumed, [2 + w] arrivals
   __nv_bfloat16* tp_out[kTpMaxRanks];            // bf16 [M, N], row stride tp_ldo, per rank
   int64_t tp_ldo;
 };
@@ -209,6 +211,7 @@ enum WaitSite : uint32_t {
 // `pieces` parts (pieces > 1: partial sums meet in the workspace).
 struct UnitCoord {
   int tile, tr, tc, kt0, kt1, split, pieces;
+  int stile;  // the tile's place in the schedule (= tile unless a row-parallel rank rotates it)
 };
 
 // Two schedules of a CTA's units.
@@ -257,6 +260,8 @@ __device__ __forceinline__ UnitCoord unit_coord(const GemmParams& p, int u, int 
     c.kt1 = min(p.k_tiles, c.kt0 + p.k_per_split);
     c.pieces = p.splits;
   }
+  c.stile = c.tile;
+  if (p.tp_rot) c.tile = (c.tile + p.tp_rot) % p.tiles;
   const int span = p.group_r * p.tiles_c;
   const int first = (c.tile / span) * p.group_r;
   const int rows = min(p.tiles_r - first, p.group_r);
@@ -266,7 +271,7 @@ __device__ __forceinline__ UnitCoord unit_coord(const GemmParams& p, int u, int 
 }
 
 __device__ __forceinline__ int next_unit(const GemmParams& p, int u, const UnitCoord& c, int scount) {
-  return p.sk_grid > 0 ? c.tile * p.k_tiles + c.kt1 : u + scount;
+  return p.sk_grid > 0 ? c.stile * p.k_tiles + c.kt1 : u + scount;
 }
 
 template <int N>
@@ -717,11 +722,12 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
       const int W = p.tp_world;
       const int wtile = PAIR ? c.tile * 2 + int(rank) : c.tile;
       const int64_t wtiles = int64_t(p.tiles) * (PAIR ? 2 : 1);
-      const int owner = wtile % W;
+      const int owner = int(int64_t(c.tile) * W / p.tiles);
       const int64_t rank_stride = wtiles * (128 * BN);
       // Column j of this thread's accumulators is tile column cidx(j).
       auto cidx = [&](int j) { return SWAP ? j : g * COLS + j; };
       float* slots = p.tp_partials[owner] + int64_t(wtile) * (128 * BN) + row;
+      unsigned long long* cnt = p.tp_counters[owner] + 2 + wtile;
       if (row_ok && cols_ok && ok) {
         float* w = slots + p.tp_rank * rank_stride;
 #pragma unroll
@@ -729,8 +735,9 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
       }
       named_bar_sync(1, Cfg::EPI_THREADS);
       if (ew == 0 && lane == 0) {
-        fence_acq_rel_sys();  // every thread's partial (ordered by the barrier) before the count
-        unsigned long long* cnt = p.tp_counters[owner] + 1 + wtile;
+        // Release (system scope): every epilogue thread's partial, ordered
+        // before this by the barrier, is visible to whoever acquires the
+        // count; acquire: the other ranks' partials are visible to us.
         const bool last = atom_add_acq_rel_sys(cnt, 1ull) == static_cast<unsigned long long>(W - 1);
         // Reset for the next call: no rank counts on this tile again before
         // it has seen this tile delivered (its kernel waits for that).
@@ -740,7 +747,9 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
       named_bar_sync(1, Cfg::EPI_THREADS);
       if (*last_flag == 0) return;
       if (row_ok && cols_ok && ok) {
-        // Sum the ranks' partials in rank order from zero, round once to bf16.
+        // Sum the ranks' partials in rank order from zero, round once to bf16
+        // (the owner's schedule reaches its tiles last, so this is usually
+        // the owner reading its own memory).
 #pragma unroll
         for (int j = 0; j < COLS; ++j) accum[j] = 0.f;
         for (int s = 0; s < W; ++s) {
@@ -770,7 +779,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
       }
       named_bar_sync(1, Cfg::EPI_THREADS);
       if (ew == 0 && lane == 0) {
-        fence_acq_rel_sys();  // the tile's outputs before the delivery counts
+        // Release: the tile's outputs (every thread's, by the barrier) before
+        // each rank's delivery count.
         for (int q = 0; q < W; ++q) red_add_release_sys(p.tp_counters[q], 1ull);
       }
     };
@@ -1004,11 +1014,15 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
         }
       }
     }
-    if (Cfg::TP && p.tp_wait && blockIdx.x == 0 && ew == 0 && lane == 0) {
-      // This rank's output is complete once every tile has been delivered
-      // (by whichever rank summed it); the kernel ends after that.
+    if (Cfg::TP && blockIdx.x == 0 && ew == 0 && lane == 0) {
+      // This rank's output is complete once every tile half has been
+      // delivered (by whichever rank summed it): counter [0] reaches the
+      // tiles of all calls so far, counter [1] (written only here) plus
+      // this call's.  The kernel ends after that.
+      unsigned long long* mine = p.tp_counters[p.tp_rank];
+      const unsigned long long target = mine[1] + static_cast<unsigned long long>(p.tiles) * (PAIR ? 2 : 1);
       const uint64_t t0 = globaltimer();
-      while (ld_acquire_sys(p.tp_counters[p.tp_rank]) < p.tp_done_target) {
+      while (p.tp_wait && ld_acquire_sys(mine) < target) {
         if (*abort_flag || globaltimer() - t0 > kWaitTimeoutNs) {
           record_status((0x5Bull << 56) | (uint64_t(kWaitTpDelivered) << 32) | (uint64_t(blockIdx.x) << 8) |
                         uint64_t(warp));
@@ -1016,6 +1030,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
         }
         __nanosleep(64);
       }
+      mine[1] = target;
     }
     if (lane == 0) bulk_wait0();  // stores complete before the CTA retires
   }

@@ -122,7 +122,7 @@ class RowParallelGroup:
             plan = _native.Plan(cfg, 1, 0)
             part = max(part, capi.tp_partial_bytes(probe, plan, self.world))
             tiles = max(tiles, capi.tp_tiles(probe, plan))
-        sizes = (part, 8 * (1 + tiles), 2 * max_m * n)
+        sizes = (part, 8 * (2 + tiles), 2 * max_m * n)
         self._own, handles = [], []
         with torch.cuda.device(self.device):
             for nbytes in sizes:
@@ -148,7 +148,6 @@ class RowParallelGroup:
                 self.partials.append(ptrs[0])
                 self.counters.append(ptrs[1])
                 self.outs.append(ptrs[2])
-        self.delivered = 0  # tiles delivered to each rank so far (the same on every rank)
         self._group = group
         self._scratch = {}
 
@@ -180,12 +179,10 @@ class RowParallelGroup:
             q, s = capi.quantize(x)
             p = capi.problem(q, s, b_q, b_scales, out)
         ws, cnt = capi.scratch(p, plan, self.device)
-        tiles = capi.tp_tiles(p, plan)
-        tp = _native.TpGroup(world=self.world, rank=self.rank, wait=1, done_target=self.delivered + tiles)
+        tp = _native.TpGroup(world=self.world, rank=self.rank, wait=1)
         for qr in range(self.world):
             tp.partials[qr], tp.counters[qr], tp.out[qr] = self.partials[qr], self.counters[qr], self.outs[qr]
         capi.launch_gemm_tp(p, plan, tp, ws, cnt)
-        self.delivered += tiles
         return out
 
     def close(self) -> None:

@@ -150,36 +150,36 @@ int bfp8_launch_gemm_noalloc(const bfp8_gemm_problem* p, bfp8_plan plan, void* s
  * the o and down projections of a tensor-parallel model, where vLLM's
  * RowParallelLinear calls the block-FP8 GEMM (blockfp8_vllm/kernel.py:42-61)
  * and then all-reduces the bf16 outputs.  Every rank of a group of `world`
- * GPUs launches the same problem shape and plan over its own K slice.  Each
- * tile's fp32 sum goes to one rank's partial buffer over NVLink (peer
- * stores); the rank that completes a tile's count sums the `world` partials
- * in rank order from zero, rounds once to bf16 and stores the tile into
- * every rank's output; so the result is the same on every rank and from
- * call to call.  No CTA waits for another rank inside the tile loop; with
- * wait = 1 one thread waits (bounded, about 2 s, then the device status
- * records site 8) at the end until this rank's output is complete.
+ * GPUs launches the same problem shape and plan over its own K slice.
+ * Tiles belong to ranks in contiguous blocks and each rank's schedule
+ * reaches its own block last.  A tile's fp32 sum goes to its owner's
+ * partial buffer (over NVLink for the other ranks); the arrival that
+ * completes the tile's count -- usually the owner's own -- sums the `world`
+ * partials in rank order from zero, rounds once to bf16 and stores the tile
+ * into every rank's output; so the result is the same on every rank and
+ * from call to call.  No CTA waits for another rank inside the tile loop;
+ * with wait = 1 one thread waits (bounded, about 2 s, then the device
+ * status records site 8) at the end until this rank's output is complete.
  *
  * Buffers, per rank, mapped into every other rank (bfp8_tp_alloc /
  * bfp8_tp_open):
  *   partials: bfp8_tp_partial_bytes() (with this world size) bytes;
- *   counters: 1 + bfp8_tp_tiles() unsigned 64-bit, zero at allocation:
- *             [0] counts tiles delivered to this rank (never reset), [1 + t]
+ *   counters: 2 + bfp8_tp_tiles() unsigned 64-bit, zero at allocation:
+ *             [0] tiles delivered to this rank, [1] tiles this rank has
+ *             taken (both grow by bfp8_tp_tiles() per call), [2 + t]
  *             arrivals on tile t (the kernel resets them);
  *   out:      the bf16 output [M, N] (row stride p->ldc, the same on every
  *             rank); p->c must be out[rank].
- * done_target: the value counters[0] of this rank reaches when this call's
- * tiles are in: the sum of bfp8_tp_tiles() over the group's calls so far,
- * this one included (the same on every rank).  All ranks make the same
- * calls in the same order; a call's output stays valid until the group's
- * next call.  After an error (a bounded wait gave up) the group's counters
- * are no longer consistent: make a new group.  wait = 0 leaves the ordering
- * to the caller (e.g. ranks emulated one after another on one GPU).
- * No counterpart in the reference. */
+ * The host keeps no per-call state, so a sequence of calls can be captured
+ * and replayed.  All ranks make the same calls in the same order; a call's
+ * output stays valid until the group's next call.  After an error (a
+ * bounded wait gave up) the counters are no longer consistent: make a new
+ * group.  wait = 0 leaves the ordering to the caller (e.g. ranks emulated
+ * one after another on one GPU).  No counterpart in the reference. */
 #define BFP8_TP_MAX_RANKS 8
 typedef struct bfp8_tp_group {
   int world, rank;
   int wait;
-  unsigned long long done_target;
   float* partials[BFP8_TP_MAX_RANKS];
   unsigned long long* counters[BFP8_TP_MAX_RANKS];
   void* out[BFP8_TP_MAX_RANKS];

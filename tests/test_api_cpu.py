@@ -290,7 +290,7 @@ def test_row_parallel_sizes_and_argument_checks():
     plan = _native.Plan(0, 1, 0)
 
     def launch(**kw):
-        tp = _native.TpGroup(world=kw.get("world", 2), rank=kw.get("rank", 1), wait=0, done_target=1)
+        tp = _native.TpGroup(world=kw.get("world", 2), rank=kw.get("rank", 1), wait=0)
         for q in range(8):
             tp.partials[q], tp.counters[q], tp.out[q] = 8192, 16384, 4096 + 65536 * q
         tp.out[1] = kw.get("own", 4096)

@@ -51,15 +51,14 @@ def emulate(world, a, sa, b, sb, plan, rounds=2, fused=False):
     tiles = capi.tp_tiles(probe, plan)
     part_bytes = capi.tp_partial_bytes(probe, plan, world)
     partials = [torch.zeros(part_bytes // 4, dtype=torch.float32, device=DEV) for _ in range(world)]
-    counters = [torch.zeros(1 + tiles, dtype=torch.int64, device=DEV) for _ in range(world)]
+    counters = [torch.zeros(2 + tiles, dtype=torch.int64, device=DEV) for _ in range(world)]
     outs = [torch.full((m, n), float("nan"), dtype=torch.bfloat16, device=DEV) for _ in range(world)]
     results = []
     for rnd in range(rounds):
         for r in range(world):
             p = _rank_problem(a, sa, b, sb, outs[r], *slices[r], fused)
             ws, cnt = capi.scratch(p, plan, a.device)
-            tp = _native.TpGroup(world=world, rank=r, wait=1 if world == 1 else 0,
-                                 done_target=(rnd + 1) * tiles)
+            tp = _native.TpGroup(world=world, rank=r, wait=1 if world == 1 else 0)
             for q in range(world):
                 tp.partials[q] = partials[q].data_ptr()
                 tp.counters[q] = counters[q].data_ptr()
@@ -78,7 +77,8 @@ def _check_group(results, counters, tiles, rounds):
             assert torch.equal(o.view(torch.int16), first.view(torch.int16)), "ranks or rounds differ"
     for c in counters:
         assert c[0].item() == rounds * tiles, "delivered-tile count"
-        assert torch.count_nonzero(c[1:]).item() == 0, "tile counters not reset"
+        assert c[1].item() == rounds * tiles, "taken-tile count"
+        assert torch.count_nonzero(c[2:]).item() == 0, "tile counters not reset"
     return first
 
 
@@ -155,7 +155,7 @@ def test_argument_checks():
     plan = _native.Plan(0, 1, 0)
     cnt = torch.zeros(64, dtype=torch.int64, device=DEV)
     part = torch.zeros(1 << 20, dtype=torch.float32, device=DEV)
-    tp = _native.TpGroup(world=2, rank=0, wait=0, done_target=1)
+    tp = _native.TpGroup(world=2, rank=0, wait=0)
     tp.partials[0] = tp.partials[1] = part.data_ptr()
     tp.counters[0] = tp.counters[1] = cnt.data_ptr()
     tp.out[0], tp.out[1] = other.data_ptr(), out.data_ptr()
@@ -194,6 +194,25 @@ def _two_gpu_worker(rank, world, port, results):
             out[m] = (all(torch.equal(t.view(torch.int16), y.view(torch.int16)) for t in gathered),
                       float((y.float() - full.float()).abs().max()), float((y_nccl.float() - full.float()).abs().max()),
                       float(full.float().abs().max()))
+        # The group keeps no per-call host state: a captured call replays.
+        x = (torch.randn(16, k, generator=g) * 2).to(torch.bfloat16).cuda()
+        xr = x[:, lo:hi].contiguous()
+        eager = grp.linear(xr, b_r, sb_r).clone()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            grp.linear(xr, b_r, sb_r)
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            y_graph = grp.linear(xr, b_r, sb_r)
+        replays_equal = True
+        for _ in range(3):
+            graph.replay()
+            torch.cuda.synchronize()
+            replays_equal = replays_equal and torch.equal(y_graph.view(torch.int16), eager.view(torch.int16))
+        del graph
+        out["graph"] = replays_equal
         assert _native.device_status(reset=True) == 0
         grp.close()
         if rank == 0:
@@ -212,7 +231,8 @@ def test_two_gpus_over_nvlink():
     results = mp.Manager().dict()
     port = 29500 + os.getpid() % 1000
     mp.spawn(_two_gpu_worker, args=(2, port, results), nprocs=2, join=True)
-    assert set(results.keys()) == {1, 16, 300, 512}
+    assert set(results.keys()) == {1, 16, 300, 512, "graph"}
+    assert results.pop("graph"), "graph replays differ from the eager call"
     for m, (same, err, err_nccl, amax) in results.items():
         assert same, f"ranks differ at M={m}"
         assert err <= 1e-2 * amax, (m, err, amax)
