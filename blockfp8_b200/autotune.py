@@ -6,6 +6,7 @@ quantizes inside the GEMM -- and write the winners to
 csrc/fused_plan_table.inc.
 
     python -m blockfp8_b200.autotune [--out results.json] [--write-table] [--fused-only]
+    python -m blockfp8_b200.autotune --gemm-only --tp 2,4,8 --write-table   # tensor-parallel shards
 
 Counterpart of the reference's bench/autotune.py (sweep :66-82, table
 :169-177), re-done for B200: each candidate GEMM is timed by
@@ -30,6 +31,17 @@ FUSED_TABLE = os.path.join(HERE, "csrc", "fused_plan_table.inc")
 FUSED_M = [1, 2, 4, 8, 16, 32, 64]
 QUANT_KERNEL, IN_GEMM = 1, 2
 LAYERS = {"qkv": (6144, 4096), "o": (4096, 4096), "gate_up": (24576, 4096), "down": (4096, 12288)}
+
+
+def tp_layers(degrees) -> dict:
+    """The same layers as one GPU of a tensor-parallel group sees them:
+    qkv and gate_up split along N (column-parallel), o and down along K
+    (row-parallel)."""
+    out = {}
+    for tp in degrees:
+        for name, (n, k) in LAYERS.items():
+            out[f"{name}/tp{tp}"] = (n // tp, k) if name in ("qkv", "gate_up") else (n, k // tp)
+    return out
 TUNE_M = [1, 2, 4, 8, 16, 32, 64, 128, 256, 512, 1024, 2048, 4096, 8192]
 SPLITS = [1, 2, 3, 4, 6, 8, 12, 16]  # and stream-K (negative) where the tiles fill waves unevenly
 
@@ -55,14 +67,14 @@ def candidates(m, n, k, num_configs, names, num_sms=148):
             yield config, -num_sms  # stream-K: every SM the same number of K blocks
 
 
-def sweep(calls=64, layers=None, ms=None):
+def sweep(calls=64, layers=None, ms=None, shapes=None):
     dev = torch.device("cuda", 0)
     lib = _native.capi()
     nconf = lib.bfp8_num_configs()
     names = [lib.bfp8_config_name(i).decode() for i in range(nconf)]
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
     results = []
-    for name, (n, k) in LAYERS.items():
+    for name, (n, k) in (shapes or LAYERS).items():
         if layers and name not in layers:
             continue
         g = torch.Generator(device=dev).manual_seed(0)
@@ -167,7 +179,7 @@ def write_table(results, names, merge=True) -> None:
     rows = read_table() if merge and os.path.exists(TABLE) else {}
     for r in results:
         rows[(r["n"], r["k"], r["m"])] = (r["best"]["config"], r["best"]["splits"])
-    order = {shape: i for i, shape in enumerate(LAYERS.values())}
+    order = {shape: i for i, shape in enumerate(list(LAYERS.values()) + list(tp_layers((2, 4, 8)).values()))}
     lines = ["// Generated by blockfp8_b200/autotune.py on a B200; do not edit.",
              "// Configurations: " + ", ".join(names),
              "// {N, K, M, config, splits}; splits < 0: stream-K over -splits CTAs"]
@@ -185,11 +197,14 @@ def main():
     ap.add_argument("--fused-only", action="store_true", help="keep plan_table.inc; tune the fused table")
     ap.add_argument("--gemm-only", action="store_true", help="tune plan_table.inc only")
     ap.add_argument("--ms", type=str, default=None, help="comma-separated M values of the GEMM sweep")
+    ap.add_argument("--tp", type=str, default=None,
+                    help="comma-separated tensor-parallel degrees: sweep their shard shapes instead")
     args = ap.parse_args()
     out = {}
     if not args.fused_only:
         ms = [int(v) for v in args.ms.split(",")] if args.ms else None
-        results, names = sweep(args.calls, ms=ms)
+        shapes = tp_layers([int(v) for v in args.tp.split(",")]) if args.tp else None
+        results, names = sweep(args.calls, ms=ms, shapes=shapes)
         out.update(configs=names, results=results)
         if args.write_table:
             write_table(results, names)
