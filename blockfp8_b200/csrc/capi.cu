@@ -506,10 +506,11 @@ bfp8_plan bfp8_choose_plan(int M, int N, int K, int num_sms) {
 // first weight loads overlap the quantizer (the unfused GEMM's plan), or a
 // GEMM that quantizes its own activations; the fused table says which is
 // faster where both were timed, up to its largest M for the shape.
+// A quantization-kernel entry always takes the GEMM table's current plan,
+// so the fused and unfused routes give the same bits.
 bfp8_plan bfp8_choose_fused_plan(int M, int N, int K, int num_sms) {
   if (const FusedTableEntry* t = lookup(kFusedPlanTable, kFusedPlanEntries, M, N, K))
-    if (t->m >= M && (t->mode == BFP8_FUSED_QUANT_KERNEL || t->mode == BFP8_FUSED_IN_GEMM))
-      return {t->config, t->splits, t->mode};
+    if (t->m >= M && t->mode == BFP8_FUSED_IN_GEMM) return {t->config, t->splits, t->mode};
   bfp8_plan plan = bfp8_choose_plan(M, N, K, num_sms);
   plan.fused = BFP8_FUSED_QUANT_KERNEL;
   return plan;

@@ -146,6 +146,8 @@ def test_c_abi_answers_without_a_gpu():
         assert 0 <= plan.config < n and plan.splits >= 1 and plan.fused == 0
         fplan = lib.bfp8_choose_fused_plan(m, nn, k, 148)
         assert fplan.fused in (1, 2)
+        if fplan.fused == 1:  # quantization kernel + the GEMM's own plan: same bits as unfused
+            assert (fplan.config, fplan.splits) == (plan.config, plan.splits)
         p = _native.GemmProblem(M=m, N=nn, K=k)
         tiles, kt = ctypes.c_int(), ctypes.c_int()
         assert lib.bfp8_plan_shape(ctypes.byref(p), plan, ctypes.byref(tiles), ctypes.byref(kt)) == 0
