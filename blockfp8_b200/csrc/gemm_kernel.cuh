@@ -712,77 +712,119 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
       publish_unit(c_next, 0);
     }
 
-    // Row-parallel hand-off of a tile this CTA holds whole (every epilogue
-    // thread calls it; the barriers inside are CTA-wide).  The partial goes
-    // in [column][row] order so a warp's stores and loads cover 128
-    // contiguous bytes, local or across NVLink.  No CTA waits here: the
-    // last of the world arrivals does the sum.
-    auto tp_reduce = [&](const UnitCoord& c, int r, bool row_ok, bool cols_ok, int col0, float (&accum)[COLS],
-                         bool ok) {
-      const int W = p.tp_world;
-      const int wtile = PAIR ? c.tile * 2 + int(rank) : c.tile;
-      const int64_t wtiles = int64_t(p.tiles) * (PAIR ? 2 : 1);
-      const int owner = int(int64_t(c.tile) * W / p.tiles);
-      const int64_t rank_stride = wtiles * (128 * BN);
-      // Column j of this thread's accumulators is tile column cidx(j).
-      auto cidx = [&](int j) { return SWAP ? j : g * COLS + j; };
-      float* slots = p.tp_partials[owner] + int64_t(wtile) * (128 * BN) + row;
-      unsigned long long* cnt = p.tp_counters[owner] + 2 + wtile;
+    // Row-parallel hand-off of the tiles this CTA holds whole (every
+    // epilogue thread runs these; the barriers inside are CTA-wide).  A
+    // partial goes in [column][row] order so a warp's stores and loads cover
+    // 128 contiguous bytes, local or across NVLink.  No CTA waits here for
+    // another rank: the arrival that completes a tile's count does the sum.
+    auto tp_owner = [&](const UnitCoord& c) { return int(int64_t(c.tile) * p.tp_world / p.tiles); };
+    auto tp_wtile = [&](const UnitCoord& c) { return PAIR ? c.tile * 2 + int(rank) : c.tile; };
+    const int64_t tp_rank_stride = int64_t(p.tiles) * (PAIR ? 2 : 1) * (128 * BN);
+    // Column j of a thread's accumulators is tile column tp_col(j).
+    auto tp_col = [&](int j) { return SWAP ? j : g * COLS + j; };
+    auto tp_slots = [&](const UnitCoord& c) {
+      return p.tp_partials[tp_owner(c)] + int64_t(tp_wtile(c)) * (128 * BN) + row;
+    };
+    // This rank's fp32 sum of tile c into its slot at the owner.
+    auto tp_push = [&](const UnitCoord& c, bool row_ok, bool cols_ok, float (&accum)[COLS], bool ok) {
       if (row_ok && cols_ok && ok) {
-        float* w = slots + p.tp_rank * rank_stride;
+        float* w = tp_slots(c) + p.tp_rank * tp_rank_stride;
 #pragma unroll
-        for (int j = 0; j < COLS; ++j) __stcg(w + cidx(j) * 128, accum[j]);
+        for (int j = 0; j < COLS; ++j) __stcg(w + tp_col(j) * 128, accum[j]);
       }
+    };
+    // One arrival on tile c (after every thread's push, by the barrier);
+    // true, on every thread, for the arrival that completes the count.
+    auto tp_count = [&](const UnitCoord& c) {
       named_bar_sync(1, Cfg::EPI_THREADS);
       if (ew == 0 && lane == 0) {
-        // Release (system scope): every epilogue thread's partial, ordered
-        // before this by the barrier, is visible to whoever acquires the
-        // count; acquire: the other ranks' partials are visible to us.
-        const bool last = atom_add_acq_rel_sys(cnt, 1ull) == static_cast<unsigned long long>(W - 1);
+        // Release (system scope): the pushes ordered before this by the
+        // barrier are visible to whoever acquires the count; acquire: the
+        // other ranks' pushes are visible to us.
+        unsigned long long* cnt = p.tp_counters[tp_owner(c)] + 2 + tp_wtile(c);
+        const bool last = atom_add_acq_rel_sys(cnt, 1ull) == static_cast<unsigned long long>(p.tp_world - 1);
         // Reset for the next call: no rank counts on this tile again before
         // it has seen this tile delivered (its kernel waits for that).
         if (last) st_relaxed_sys(cnt, 0ull);
         *last_flag = last;
       }
       named_bar_sync(1, Cfg::EPI_THREADS);
-      if (*last_flag == 0) return;
+      return *last_flag != 0;
+    };
+    // bf16 of v[0 .. n) (tile columns j0 ..) of row r / weight row r into every rank's output.
+    auto tp_store = [&](int r, int col0, int j0, const float* v, int n) {
+      for (int q = 0; q < p.tp_world; ++q) {
+        if constexpr (!SWAP) {
+          // Row r, 16-byte pieces (N and the row stride are multiples of 8,
+          // outputs 16-byte aligned).
+          __nv_bfloat16* o = p.tp_out[q] + int64_t(r) * p.tp_ldo + col0 + j0;
+          for (int j = 0; j < n; j += 8)
+            if (col0 + j0 + j < p.N)
+              *reinterpret_cast<uint4*>(o + j) =
+                  make_uint4(bf16x2_bits(v[j], v[j + 1]), bf16x2_bits(v[j + 2], v[j + 3]),
+                             bf16x2_bits(v[j + 4], v[j + 5]), bf16x2_bits(v[j + 6], v[j + 7]));
+        } else {
+          // Weight row r is output column r; token col0 + j is an output row.
+          __nv_bfloat16* o = p.tp_out[q] + r;
+          for (int j = 0; j < n; ++j)
+            if (col0 + j0 + j < p.M) o[int64_t(col0 + j0 + j) * p.tp_ldo] = __float2bfloat16_rn(v[j]);
+        }
+      }
+    };
+    // After the stores of a delivered tile (every thread's, by the barrier):
+    // one more on every rank's delivery count.
+    auto tp_delivered = [&]() {
+      named_bar_sync(1, Cfg::EPI_THREADS);
+      if (ew == 0 && lane == 0)
+        for (int q = 0; q < p.tp_world; ++q) red_add_release_sys(p.tp_counters[q], 1ull);
+    };
+    // The sum of tile c's partials in rank order from zero, rounded once to
+    // bf16 and delivered.  Full width, in this thread's accumulators.
+    auto tp_sum_full = [&](const UnitCoord& c, int r, bool row_ok, bool cols_ok, int col0, float (&accum)[COLS],
+                           bool ok) {
       if (row_ok && cols_ok && ok) {
-        // Sum the ranks' partials in rank order from zero, round once to bf16
-        // (the owner's schedule reaches its tiles last, so this is usually
-        // the owner reading its own memory).
 #pragma unroll
         for (int j = 0; j < COLS; ++j) accum[j] = 0.f;
-        for (int s = 0; s < W; ++s) {
-          const float* w = slots + s * rank_stride;
+        for (int s = 0; s < p.tp_world; ++s) {
+          const float* w = tp_slots(c) + s * tp_rank_stride;
 #pragma unroll
-          for (int j = 0; j < COLS; ++j) accum[j] += __ldcg(w + cidx(j) * 128);
+          for (int j = 0; j < COLS; ++j) accum[j] += __ldcg(w + tp_col(j) * 128);
         }
-        for (int q = 0; q < W; ++q) {
-          if constexpr (!SWAP) {
-            // Row r, columns col0 .. col0 + COLS - 1 in 16-byte pieces (N and
-            // the row stride are multiples of 8, outputs 16-byte aligned).
-            __nv_bfloat16* o = p.tp_out[q] + int64_t(r) * p.tp_ldo + col0;
+        tp_store(r, col0, 0, accum, COLS);
+      }
+      tp_delivered();
+    };
+    // The same for a tile handed over earlier, while the accumulators hold
+    // a newer tile: 32 columns at a time.
+    auto tp_sum_chunked = [&](const UnitCoord& c, bool ok) {
+      const int r = c.tr * Cfg::TILE_M + row_off + row;
+      const int col0 = c.tc * BN + g * COLS;
+      if (r < rows_total && col0 < (SWAP ? p.M : p.N) && ok) {
+        constexpr int CH = COLS < 32 ? COLS : 32;
+#pragma unroll 1
+        for (int j0 = 0; j0 < COLS; j0 += CH) {
+          float t[CH];
 #pragma unroll
-            for (int j = 0; j < COLS; j += 8)
-              if (col0 + j < p.N)
-                *reinterpret_cast<uint4*>(o + j) = make_uint4(
-                    bf16x2_bits(accum[j], accum[j + 1]), bf16x2_bits(accum[j + 2], accum[j + 3]),
-                    bf16x2_bits(accum[j + 4], accum[j + 5]), bf16x2_bits(accum[j + 6], accum[j + 7]));
-          } else {
-            // Weight row r is output column r; token col0 + j is output row.
-            __nv_bfloat16* o = p.tp_out[q] + r;
+          for (int j = 0; j < CH; ++j) t[j] = 0.f;
+          for (int s = 0; s < p.tp_world; ++s) {
+            const float* w = tp_slots(c) + s * tp_rank_stride;
 #pragma unroll
-            for (int j = 0; j < COLS; ++j)
-              if (col0 + j < p.M) o[int64_t(col0 + j) * p.tp_ldo] = __float2bfloat16_rn(accum[j]);
+            for (int j = 0; j < CH; ++j) t[j] += __ldcg(w + tp_col(j0 + j) * 128);
           }
+          tp_store(r, col0, j0, t, CH);
         }
       }
-      named_bar_sync(1, Cfg::EPI_THREADS);
-      if (ew == 0 && lane == 0) {
-        // Release: the tile's outputs (every thread's, by the barrier) before
-        // each rank's delivery count.
-        for (int q = 0; q < W; ++q) red_add_release_sys(p.tp_counters[q], 1ull);
-      }
+      tp_delivered();
+    };
+    // A tile of another rank is counted only at the end of this CTA's next
+    // tile (or of the kernel): its pushes cross NVLink meanwhile, so the
+    // release of the count does not wait for them.  A rank's own tiles are
+    // counted at once (local pushes, and usually the completing arrival).
+    UnitCoord tp_pending{};
+    bool tp_has_pending = false;
+    auto tp_flush = [&](bool ok) {
+      if (tp_has_pending && tp_count(tp_pending)) tp_sum_chunked(tp_pending, ok);
+      tp_has_pending = false;
     };
 
     int next_seq = 0;  // position of the next unit's first K block in the CTA's sequence
@@ -970,7 +1012,16 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
       }
 
       if constexpr (Cfg::TP) {
-        if (tile_whole) tp_reduce(c, r, row_ok, cols_ok, col0, accum, ok);  // CTA-uniform
+        if (tile_whole) {  // CTA-uniform
+          tp_flush(ok);    // the previous tile of another rank, before this tile's pushes
+          tp_push(c, row_ok, cols_ok, accum, ok);
+          if (tp_owner(c) == p.tp_rank) {
+            if (tp_count(c)) tp_sum_full(c, r, row_ok, cols_ok, col0, accum, ok);
+          } else {
+            tp_pending = c;
+            tp_has_pending = true;
+          }
+        }
       } else if (store && ok) {
         if constexpr (!SWAP) {
           // bf16 rows -> [32 x 32] chunks, 64-byte swizzle, two buffers in
@@ -1014,6 +1065,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
         }
       }
     }
+    if constexpr (Cfg::TP) tp_flush(ok);
     if (Cfg::TP && blockIdx.x == 0 && ew == 0 && lane == 0) {
       // This rank's output is complete once every tile half has been
       // delivered (by whichever rank summed it): counter [0] reaches the
