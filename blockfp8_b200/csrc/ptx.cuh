@@ -195,8 +195,6 @@ __device__ __forceinline__ void griddep_launch_dependents() {
 }
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
-// gpu-scope acquire-release fence (split-K counter hand-off).
-__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 // A read-only global load the compiler keeps where it is written (a prefetch
 // must go out early, not next to its use).
 __device__ __forceinline__ float ldg_pinned(const float* ptr) {
@@ -213,7 +211,6 @@ __device__ __forceinline__ int atom_add_acq_rel_gpu(int* ptr, int v) {
 
 // System-scope versions for the row-parallel reduction, whose partial sums,
 // counters and outputs live in other GPUs' memory (NVLink peer mappings).
-__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 __device__ __forceinline__ unsigned long long atom_add_acq_rel_sys(unsigned long long* ptr,
                                                                    unsigned long long v) {
   unsigned long long old;
