@@ -306,3 +306,19 @@ def test_row_parallel_sizes_and_argument_checks():
     assert "aligned" in launch(own=4100)[1]
     rc, msg = launch()  # a valid group: the first CUDA call fails here (no device)
     assert rc == _native.BFP8_ECUDA, msg
+
+
+def test_plan_table_rows_are_layer_or_shard_shapes():
+    """Every tuned row is a Qwen3-8B linear or one GPU's shard of it under
+    tensor parallelism 2/4/8 (autotune --tp), with a valid plan."""
+    from blockfp8_b200 import autotune
+
+    shapes = set(autotune.LAYERS.values()) | set(autotune.tp_layers((2, 4, 8)).values())
+    assert autotune.tp_layers((2,))["qkv/tp2"] == (3072, 4096)
+    assert autotune.tp_layers((2,))["down/tp2"] == (4096, 6144)
+    rows = autotune.read_table()
+    lib = _native.capi()
+    assert rows and all((n, k) in shapes for n, k, _ in rows)
+    for (n, k, m), (config, splits) in rows.items():
+        assert 0 <= config < lib.bfp8_num_configs() and splits != 0
+        assert lib.bfp8_choose_plan(m, n, k, 148).config == config or m >= 256  # exact rows are returned as tuned
