@@ -3,7 +3,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...        (N > 1)
 
-Headline workload (the one defined at 1/2/4/8 GPUs): the
+Headline workload (the benchmark configuration defined at 1/2/4/8 GPUs): the
 Qwen3-8B gate_up projection as one blockfp8 linear call -- the activation
 quantizer plus the block-scaled GEMM -- M = 8192, N = 24576, K = 4096, with
 N split into contiguous multiple-of-128 slices, one per GPU, and x
@@ -18,9 +18,9 @@ torch.cuda.synchronize() on both sides of the K timed steps; nvidia-smi
 samples the clocks during them.
 
 At N = 1, rank 0 also reports:
-  decode   BASELINE config 2: the four Qwen3-8B shapes x M in {1..32}, linear
+  decode   the four Qwen3-8B shapes x M in {1..32}, linear
            time and weight GB/s = (N K + 4 nb kb) / t against HBM;
-  prefill  BASELINE config 3: the four shapes x M in {100 .. 8192}, linear
+  prefill  the four shapes x M in {100 .. 8192} (off-grid M included), linear
            and GEMM-only TFLOPS;
   roofline of the dominant kernel (the GEMM) and cpu_baseline (the CPU
            oracle on a row sample of the same workload, timed on this host).

@@ -6,7 +6,7 @@ import torch
 from oracle import oracle as O
 
 FP8 = torch.float8_e4m3fn
-# BASELINE parity contract for the GEMM output: |C - ref| <= RTOL |ref| + ATOL max|ref|.
+# Parity contract for the GEMM output: |C - ref| <= RTOL |ref| + ATOL max|ref|.
 RTOL = 1e-2
 ATOL_REL_MAX = 1e-2
 

@@ -1,5 +1,5 @@
 """Parity through the C ABI alone (ctypes on libblockfp8_b200.so, no torch ops),
-against the CPU oracle, on the BASELINE shapes.
+against the CPU oracle, on the Qwen3-8B linear shapes of the benchmark.
 
 Sizes: the four Qwen3-8B linear shapes at decode M (full outputs checked
 against the oracle) and at prefill M (a row sample against the oracle, plus
