@@ -94,9 +94,11 @@ class RowParallelGroup:
     construction).  All ranks must then make the same linear() calls in the
     same order, each with its own K slice (block_slices(k, world, rank)) of x
     and of the weight; every rank runs the same plan (tile ids must agree),
-    chosen for the widest slice.  The
-    returned [M, N] tensor lives in the group's output buffer: the same bits
-    on every rank, valid until the group's next call (clone it to keep it).
+    chosen for the widest slice.  The returned [M, N] tensor lives in the
+    group's output buffer: the same bits on every rank, valid until the
+    group's next call (clone it to keep it).  If a rank stops calling, the
+    others' kernels give up their bounded wait after about 2 s and
+    _native.device_status() reports it; the group must then be rebuilt.
     """
 
     def __init__(self, max_m: int, n: int, k: int, group=None, device=None):
@@ -149,7 +151,6 @@ class RowParallelGroup:
                 self.counters.append(ptrs[1])
                 self.outs.append(ptrs[2])
         self._group = group
-        self._scratch = {}
 
     def linear(self, x: torch.Tensor, b_q: torch.Tensor, b_scales: torch.Tensor) -> torch.Tensor:
         """sum over ranks of x_r @ W_r^T for this rank's x_r [M, K_r] (bf16) and
