@@ -60,6 +60,14 @@
 // leader's commits arrive on both CTAs' barriers.  Per SM a stage is 32 KB
 // instead of 48 KB, so six stages fit.
 //
+// Row-parallel twins (TP): every configuration is also compiled for a group
+// of GPUs that each hold a K slice of the same [M, N] product.  Instead of
+// storing bf16, a tile's fp32 sum goes to the owning rank's partial buffer
+// (NVLink peer memory); the arrival that completes the tile's count sums
+// the ranks' partials in rank order and stores the bf16 tile into every
+// rank's output (GemmParams tp_*).  No CTA waits for another rank inside the
+// tile loop; one thread waits, bounded, at the end for this rank's output.
+//
 // Every mbarrier wait is bounded (ptx.cuh): on a timeout the kernel records a
 // status code, drains its in-flight copies and MMAs, frees TMEM and returns.
 #pragma once
