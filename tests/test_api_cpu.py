@@ -322,3 +322,14 @@ def test_plan_table_rows_are_layer_or_shard_shapes():
     for (n, k, m), (config, splits) in rows.items():
         assert 0 <= config < lib.bfp8_num_configs() and splits != 0
         assert lib.bfp8_choose_plan(m, n, k, 148).config == config or m >= 256  # exact rows are returned as tuned
+
+
+def test_untabulated_decode_shapes_take_swapped_configurations():
+    """The planner's fallback (no tuned row for the shape) keeps to the
+    swapped decode configurations up to 32 tokens, as the tuned shapes do."""
+    lib = _native.capi()
+    names = [lib.bfp8_config_name(i).decode() for i in range(lib.bfp8_num_configs())]
+    for n, k in [(3200, 4096), (5120, 5120), (13824, 5120), (392, 1152)]:
+        for m in (1, 5, 16, 32):
+            plan = lib.bfp8_choose_plan(m, n, k, 148)
+            assert names[plan.config].startswith("w"), (n, k, m, names[plan.config])
