@@ -25,9 +25,12 @@ At N = 1, rank 0 also reports:
   roofline of the dominant kernel (the GEMM) and cpu_baseline (the CPU
            oracle on a row sample of the same workload, timed on this host).
 
---impl reference times the reference's algorithm on the host CPU (the
-oracle port in oracle/: the C quantizer + float64 BLAS GEMM, all host
-threads) on a bounded row sample of the same workload, same metric.
+--impl reference times the reference's own CPU implementation of the path
+-- blockfp8.quant.quantize_activations + blockfp8.reference.reference_gemm,
+pure torch, installed unmodified from the reference checkout into
+baseline/_ref -- on all host threads, on a bounded row sample of the same
+workload, same metric.  Without baseline/_ref it falls back to the oracle
+port in oracle/ and says so.
 """
 
 import argparse
@@ -257,30 +260,72 @@ def run_cpu_baseline(rows=REF_SAMPLE_ROWS, reps=2):
                       f"median of {reps}, {sec:.2f} s per sample"}
 
 
+def reference_path():
+    """The reference's own quantize_activations and reference_gemm, imported
+    from baseline/_ref (the unmodified reference package), or None."""
+    path = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(path, "blockfp8")):
+        return None
+    sys.path.insert(0, path)
+    for name in [m for m in sys.modules if m == "blockfp8" or m.startswith("blockfp8.")]:
+        del sys.modules[name]
+    import blockfp8.quant as quant
+    import blockfp8.reference as reference
+    if not os.path.realpath(quant.__file__).startswith(os.path.realpath(path)):
+        return None
+    return quant, reference
+
+
 def run_reference(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    O, xbits, b, sb, n, k = cpu_sample(REF_SAMPLE_ROWS)
-    with all_host_threads():
+    name, m = HEADLINE
+    n, k = LAYERS[name]
+    rows = REF_SAMPLE_ROWS
+    ref = reference_path()
+    if ref is not None:
+        quant, reference = ref
+        torch.set_num_threads(cpu_threads())
+        x = make_x(m, k, seed=0)[:rows]
+        w = torch.randn(n, k, generator=torch.Generator().manual_seed(0)) * 0.02
+        b, sb = quant.quantize_weights(w)  # operand preparation, not timed
+
+        def step():
+            a, sa = quant.quantize_activations(x)
+            return reference.reference_gemm(a, sa, b, sb)
+
+        kind, cores = "reference", torch.get_num_threads()
+        what = ("the reference's blockfp8.quant.quantize_activations + blockfp8.reference.reference_gemm "
+                "(torch, float64) from baseline/_ref")
         for _ in range(max(1, args.warmup)):
-            cpu_step(O, xbits, b, sb)
+            step()
         t0 = time.perf_counter()
         for _ in range(args.steps):
-            cpu_step(O, xbits, b, sb)
+            step()
         sec = (time.perf_counter() - t0) / args.steps
-    value = 2 * REF_SAMPLE_ROWS * n * k / sec / 1e12
-    name, m = HEADLINE
+    else:
+        O, xbits, b, sb, n, k = cpu_sample(rows)
+        kind, cores = "port", cpu_threads()
+        what = "the oracle port (baseline/_ref missing): C quantizer + float64 BLAS GEMM"
+        with all_host_threads():
+            for _ in range(max(1, args.warmup)):
+                cpu_step(O, xbits, b, sb)
+            t0 = time.perf_counter()
+            for _ in range(args.steps):
+                cpu_step(O, xbits, b, sb)
+            sec = (time.perf_counter() - t0) / args.steps
+    value = 2 * rows * n * k / sec / 1e12
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOPS",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "f64 (the reference's CPU oracle)", "data": "synthetic (seeded N(0,1) x, N(0,0.02) w)",
-        "config": {"workload": f"{name} linear M={m} N={n} K={k}, a row sample per step", "M": m,
-                   "N": n, "K": k, "sample_rows": REF_SAMPLE_ROWS},
-        "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": cpu_threads(), "kind": "port",
-                         "sample": f"{REF_SAMPLE_ROWS} of {m} rows per step"},
+        "dtype": "f64 (the reference's CPU path)", "data": "synthetic (seeded N(0,1) x, N(0,0.02) w)",
+        "config": {"workload": f"{name} linear M={m} N={n} K={k}, a sample of {rows} activation rows per "
+                               f"step (host CPU)", "M": m, "N": n, "K": k, "sample_rows": rows},
+        "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": cores, "kind": kind,
+                         "sample": f"{rows} of {m} rows per step: {what}"},
         "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

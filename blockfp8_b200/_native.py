@@ -77,6 +77,8 @@ _SIGNATURES = {
     "bfp8_choose_plan": ([ctypes.c_int] * 4, Plan),
     "bfp8_choose_fused_plan": ([ctypes.c_int] * 4, Plan),
     "bfp8_prefers_fused": ([ctypes.c_int] * 3, ctypes.c_int),
+    "bfp8_choose_tp_plan": ([ctypes.c_int] * 5, Plan),
+    "bfp8_set_weight_prefetch": ([ctypes.c_int], ctypes.c_int),
     "bfp8_plan_shape": ([ctypes.POINTER(GemmProblem), Plan, ctypes.POINTER(ctypes.c_int),
                          ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
     "bfp8_workspace_bytes": ([ctypes.POINTER(GemmProblem), Plan], ctypes.c_int64),
@@ -99,6 +101,8 @@ _SIGNATURES = {
     "bfp8_probe_hbm_read": ([ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.POINTER(ctypes.c_double)],
                             ctypes.c_int),
     "bfp8_probe_block": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
+    "bfp8_probe_quantizer": ([ctypes.c_float, ctypes.POINTER(ctypes.c_ulonglong), ctypes.POINTER(ctypes.c_ulonglong)],
+                             ctypes.c_int),
 }
 
 _capi = None
@@ -199,3 +203,11 @@ def probe_block(a, b):
                                   ctypes.c_void_p(b.contiguous().data_ptr()), ctypes.c_void_p(d.data_ptr()),
                                   ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
     return d
+
+
+def probe_quantizer(eps: float = 1e-10) -> tuple[int, int]:
+    """(mismatching codes, first mismatch) of the quantizer's fast path against
+    the reference's division sequence over the whole bf16 input domain."""
+    bad, first = ctypes.c_ulonglong(), ctypes.c_ulonglong()
+    check(capi().bfp8_probe_quantizer(eps, ctypes.byref(bad), ctypes.byref(first)))
+    return bad.value, first.value

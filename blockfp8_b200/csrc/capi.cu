@@ -26,6 +26,7 @@
 #include "gemm_kernel.cuh"
 #include "probes.cuh"
 #include "quantize.cuh"
+#include "stream_gemm.cuh"
 
 namespace bfp8 {
 namespace {
@@ -65,6 +66,14 @@ struct ConfigEntry {
   const void* kernel_fused_tp = nullptr;
   void (*launch_fused_tp)(const GemmParams&, int grid, cudaStream_t) = nullptr;
   int act_kb = 0;  // K blocks of one unit the in-kernel variant keeps resident
+  // Weight-streaming configurations (stream_gemm.cuh): at most max_m tokens,
+  // stream-K over the SMs, activations resident; no row-parallel twin.
+  bool stream = false;
+  int max_m = 0;
+  const void* kernel_stream = nullptr;  // [0] quantized activations, [1] bf16 (in-kernel quantization)
+  const void* kernel_stream_q = nullptr;
+  void (*launch_stream)(const StreamParams&, int grid, int smem, bool pdl, cudaStream_t) = nullptr;
+  void (*launch_stream_q)(const StreamParams&, int grid, int smem, bool pdl, cudaStream_t) = nullptr;
 };
 
 template <class Cfg>
@@ -76,7 +85,7 @@ void launch_cfg(const GemmParams& gp, int grid, cudaStream_t stream) {
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   int n = 0;
-  if (gp.pdl) {  // only right behind our own quantizer
+  if (!Cfg::FUSE) {  // these variants wait before reading activations (in-kernel quantization does not)
     attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[n++].val.programmaticStreamSerializationAllowed = 1;
   }
@@ -113,9 +122,40 @@ ConfigEntry entry_fused(const char* name) {
   return e;
 }
 
+template <class Cfg>
+void launch_stream_cfg(const StreamParams& sp, int grid, int smem, bool pdl, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(Cfg::THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaLaunchKernelEx(&cfg, stream_kernel<Cfg>, sp);
+}
+
+template <int BN>
+ConfigEntry entry_stream(const char* name) {
+  using C = StreamCfg<BN, false>;
+  using Q = StreamCfg<BN, true>;
+  ConfigEntry e{name, BN, 0, C::THREADS, 0, true, 128, false, nullptr, nullptr};
+  e.stream = true;
+  e.max_m = BN;
+  e.kernel_stream = reinterpret_cast<const void*>(&stream_kernel<C>);
+  e.kernel_stream_q = reinterpret_cast<const void*>(&stream_kernel<Q>);
+  e.launch_stream = &launch_stream_cfg<C>;
+  e.launch_stream_q = &launch_stream_cfg<Q>;
+  return e;
+}
+
 // Normal order: "m128n<BN>": 128 activation rows x BN weight rows per tile;
 // "m256n256": 256 x 256 tiles on a CTA pair (cta_group::2, prefill).
 // Swapped order: "w128t<BN>": 128 weight rows x BN tokens per tile (decode).
+// Weight streaming: "w128d<BN>": the swapped order for at most BN tokens,
+// every SM streaming an equal share of the weight tiles (stream_gemm.cuh).
 //                        BN  stages  swapped
 using Cfg256 = GemmCfg<256, 4, false>;
 using Cfg128 = GemmCfg<128, 6, false>;
@@ -139,6 +179,9 @@ const ConfigEntry kConfigs[] = {
     entry_fused<CfgW32, CfgW32Q>("w128t32s10"),
     entry_fused<CfgW64, CfgW64Q>("w128t64s8"),
     entry<CfgP256>("m256n256s6"),
+    entry_stream<16>("w128d16"),
+    entry_stream<32>("w128d32"),
+    entry_stream<64>("w128d64"),
 };
 constexpr int kNumConfigs = int(sizeof(kConfigs) / sizeof(kConfigs[0]));
 // The fused path (gemm_bf16) quantizes into the workspace, then runs the
@@ -171,16 +214,25 @@ int current_device_sms(int* dev_out) {
 
 // The dynamic shared-memory limit is a per-device attribute of a kernel:
 // set it on the first launch of each configuration on each device.
+// Weight-streaming kernels size their shared memory per launch, up to this.
+constexpr int kMaxSmem = 232448;
+
 int ensure_smem_attr(int config, int dev, bool in_kernel_quant, bool tp = false) {
   static std::atomic<uint64_t> done[4][kNumConfigs] = {};
   const uint64_t bit = dev < 64 ? (uint64_t(1) << dev) : 0;
   std::atomic<uint64_t>& d = done[(in_kernel_quant ? 1 : 0) + (tp ? 2 : 0)][config];
   if (bit && (d.load(std::memory_order_acquire) & bit)) return BFP8_OK;
   const ConfigEntry& e = kConfigs[config];
-  const void* kernel = in_kernel_quant ? (tp ? e.kernel_fused_tp : e.kernel_fused) : (tp ? e.kernel_tp : e.kernel);
+  const void* kernel = e.stream ? (in_kernel_quant ? e.kernel_stream_q : e.kernel_stream)
+                                : in_kernel_quant ? (tp ? e.kernel_fused_tp : e.kernel_fused)
+                                                  : (tp ? e.kernel_tp : e.kernel);
   cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         in_kernel_quant ? e.smem_fused : e.smem);
+                                         e.stream ? kMaxSmem : in_kernel_quant ? e.smem_fused : e.smem);
   if (err != cudaSuccess) return cuda_fail(err, "cudaFuncSetAttribute(MaxDynamicSharedMemorySize)");
+  if (e.stream) {  // two CTAs of up to 112 KB on one SM
+    err = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaFuncSetAttribute(PreferredSharedMemoryCarveout)");
+  }
   d.fetch_or(bit, std::memory_order_release);
   return BFP8_OK;
 }
@@ -202,6 +254,7 @@ Derived derive(const bfp8_gemm_problem& p, const bfp8_plan& plan);
 // results either way).
 bool quantizes_in_kernel(const bfp8_gemm_problem& p, const bfp8_plan& plan) {
   const ConfigEntry& e = kConfigs[plan.config];
+  if (e.stream) return plan.fused == BFP8_FUSED_IN_GEMM;
   return plan.fused == BFP8_FUSED_IN_GEMM && e.launch_fused != nullptr &&
          derive(p, plan).k_per_split <= e.act_kb;
 }
@@ -285,6 +338,13 @@ const E* lookup(const E* table, int n_entries, int M, int N, int K) {
 // two units (and partial round trips) per CTA.
 double plan_cost_ns(int M, int N, int K, int num_sms, int config, int splits) {
   const ConfigEntry& e = kConfigs[config];
+  if (e.stream) {  // the weights at HBM rate over the CTAs that stream them, plus fill and tail
+    if (M > e.max_m) return 1e300;
+    const int64_t work = int64_t(cdiv(N, 128)) * cdiv(K, 128);
+    const int64_t g = splits < 0 ? std::min<int64_t>(-int64_t(splits), work) : std::min<int64_t>(work, int64_t(cdiv(N, 128)) * splits);
+    const double share = double(std::min<int64_t>(g, num_sms)) / num_sms;
+    return double(N) * K / (6500.0 * std::max(share, 1e-3)) + 3000.0;
+  }
   const int k_tiles = cdiv(K, 128);
   const int rows_total = e.swap ? N : M, cols_total = e.swap ? M : N;
   const int tiles_r = cdiv(rows_total, e.bm), tiles_c = cdiv(cols_total, e.bn);
@@ -337,6 +397,7 @@ bfp8_plan heuristic_plan(int M, int N, int K, int num_sms, bool fused) {
   double best_t = 1e300;
   const int k_tiles = cdiv(K, 128);
   for (int config = 0; config < kNumConfigs; ++config) {
+    if (kConfigs[config].stream) continue;  // chosen by stream_plan, not by this model
     if (M <= kSwappedOnlyM && !kConfigs[config].swap) continue;
     for (int splits = 0; splits <= std::min(k_tiles, 16); ++splits) {
       if (splits == 0) {  // stream-K over every SM
@@ -384,9 +445,29 @@ Derived derive(const bfp8_gemm_problem& p, const bfp8_plan& plan) {
   const ConfigEntry& e = kConfigs[plan.config];
   Derived d;
   d.tiles_r = cdiv(e.swap ? p.N : p.M, e.bm);
-  d.tiles_c = cdiv(e.swap ? p.M : p.N, e.bn);
+  d.tiles_c = e.stream ? 1 : cdiv(e.swap ? p.M : p.N, e.bn);
   d.tiles = d.tiles_r * d.tiles_c;
   d.k_tiles = cdiv(p.K, 128);
+  if (e.stream) {
+    // Weight streaming: always one contiguous range of the tiles' K blocks
+    // per CTA; `splits` K splits per tile ask for tiles * splits CTAs,
+    // negative splits for -splits CTAs.
+    const int64_t W = int64_t(d.tiles) * d.k_tiles;
+    const int64_t want = plan.splits > 0 ? int64_t(d.tiles) * std::min(plan.splits, d.k_tiles) : -int64_t(plan.splits);
+    Derived s = d;
+    const int64_t G = std::max<int64_t>(1, std::min<int64_t>(want, W));
+    s.sk_grid = int(G);
+    s.sk_work = W;
+    s.k_per_split = int((W + G - 1) / G);  // the longest range (positions)
+    auto starts_upto = [&](int64_t x) { return std::min<int64_t>(G, ((x + 1) * G + W - 1) / W); };
+    int most = 1;
+    for (int t = 0; t < d.tiles; ++t) {
+      const int64_t t0 = int64_t(t) * d.k_tiles;
+      most = std::max(most, int(starts_upto(t0 + d.k_tiles - 1) - starts_upto(t0) + 1));
+    }
+    s.splits = most;
+    return s;
+  }
   if (plan.splits < 0) {
     // Stream-K: CTA b takes K-block positions [W b / G, W (b + 1) / G); the
     // CTAs starting at or before position x number min(G, ceil((x + 1) G / W)).
@@ -422,6 +503,8 @@ int64_t splitk_bytes(const bfp8_gemm_problem& p, const bfp8_plan& plan) {
   const Derived d = derive(p, plan);
   if (d.splits == 1) return 0;
   const ConfigEntry& e = kConfigs[plan.config];
+  // weight streaming: [tiles][parts][128 rows][M tokens rounded up to 4] fp32
+  if (e.stream) return int64_t(d.tiles) * d.splits * 128 * ((p.M + 3) & ~3) * int64_t(sizeof(float));
   // one fp32 partial per 128-row tile (a CTA pair's tile has two)
   return int64_t(d.splits) * d.tiles * (e.bm / 128) * 128 * e.bn * int64_t(sizeof(float));
 }
@@ -445,11 +528,35 @@ int check_problem(const bfp8_gemm_problem& p, bool fused) {
   return BFP8_OK;
 }
 
+// Weight tiles (and their scales) may be requested before the previous
+// kernel of the stream has finished (programmatic dependent launch); on by
+// default, see bfp8_set_weight_prefetch.
+std::atomic<int> g_weight_prefetch{1};
+
+// Every launch carries the programmatic-serialization attribute, so that it
+// can start while the previous kernel of the stream finishes; each kernel
+// waits (griddepcontrol.wait) before it reads anything a previous kernel
+// may write and before it writes anything.
+void set_pdl(cudaLaunchConfig_t& cfg, cudaLaunchAttribute* attr) {
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+}
+
 int launch_quant(const QuantParams& qp, cudaStream_t stream, int num_sms) {
   const int64_t tasks = int64_t(cdiv(qp.M, kQuantRows)) * cdiv(qp.kb, kQuantGroups);
   if (tasks == 0) return BFP8_OK;
-  const int grid = int(std::min<int64_t>(tasks, int64_t(num_sms) * 8));
-  quantize_kernel<<<grid, kQuantThreads, 0, stream>>>(qp);
+  if (tasks >= (int64_t(1) << 31)) return fail(BFP8_EINVAL, "too many rows x K groups for one quantization launch");
+  // As many CTAs as are resident at once (four per SM at this register use).
+  const int grid = int(std::min<int64_t>(tasks, int64_t(num_sms) * 4));
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kQuantThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  set_pdl(cfg, attr);
+  cudaLaunchKernelEx(&cfg, quantize_kernel, qp);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "quantize kernel launch");
   return BFP8_OK;
@@ -480,6 +587,25 @@ int static_scratch(int dev, unsigned char** out) {
   return BFP8_OK;
 }
 
+// Decode batches (up to kStreamMaxM tokens) go to the weight-streaming
+// configurations: the smallest token tile that holds M, stream-K over every
+// SM.  The linear path quantizes inside that kernel up to
+// kStreamInGemmMaxM tokens (no quantization kernel between calls); beyond,
+// two warps per CTA quantizing every K block of its range cost more than the
+// quantization kernel ahead of it (measured on B200), which it then uses.
+constexpr int kStreamMaxM = 32;
+constexpr int kStreamInGemmMaxM = 4;
+
+bfp8_plan stream_plan(int M, int N, int K, int num_sms) {
+  (void)N;
+  (void)K;
+  int best = -1;
+  for (int c = 0; c < kNumConfigs; ++c)
+    if (kConfigs[c].stream && kConfigs[c].max_m >= M && (best < 0 || kConfigs[c].max_m < kConfigs[best].max_m))
+      best = c;
+  return {best, -std::max(1, num_sms), 0};
+}
+
 }  // namespace
 }  // namespace bfp8
 
@@ -500,6 +626,7 @@ const char* bfp8_fused_config_name(int config) {
 }
 
 bfp8_plan bfp8_choose_plan(int M, int N, int K, int num_sms) {
+  if (M > 0 && M <= kStreamMaxM) return stream_plan(M, N, K, num_sms);
   if (const TableEntry* t = lookup(kPlanTable, kPlanEntries, M, N, K)) {
     t = balanced_entry(t, M, N, K, num_sms);
     return {t->config, t->splits, 0};
@@ -515,6 +642,11 @@ bfp8_plan bfp8_choose_plan(int M, int N, int K, int num_sms) {
 // A quantization-kernel entry always takes the GEMM table's current plan,
 // so the fused and unfused routes give the same bits.
 bfp8_plan bfp8_choose_fused_plan(int M, int N, int K, int num_sms) {
+  if (M > 0 && M <= kStreamMaxM) {
+    bfp8_plan plan = stream_plan(M, N, K, num_sms);
+    plan.fused = M <= kStreamInGemmMaxM ? BFP8_FUSED_IN_GEMM : BFP8_FUSED_QUANT_KERNEL;
+    return plan;
+  }
   if (const FusedTableEntry* t = lookup(kFusedPlanTable, kFusedPlanEntries, M, N, K))
     if (t->m >= M && t->mode == BFP8_FUSED_IN_GEMM) return {t->config, t->splits, t->mode};
   bfp8_plan plan = bfp8_choose_plan(M, N, K, num_sms);
@@ -526,11 +658,33 @@ bfp8_plan bfp8_choose_fused_plan(int M, int N, int K, int num_sms) {
 // is the same two kernels, overlapped), so linear always takes it.
 int bfp8_prefers_fused(int M, int N, int K) { return M >= 0 && N > 0 && K > 0 ? 1 : 0; }
 
+// The tile configurations only (those with a row-parallel twin).
+bfp8_plan bfp8_choose_tp_plan(int M, int N, int K, int num_sms, int fused) {
+  if (const TableEntry* t = lookup(kPlanTable, kPlanEntries, M, N, K))
+    if (!kConfigs[t->config].stream) {
+      t = balanced_entry(t, M, N, K, num_sms);
+      if (!kConfigs[t->config].stream) return {t->config, t->splits, fused ? BFP8_FUSED_QUANT_KERNEL : 0};
+    }
+  return heuristic_plan(M, N, K, num_sms, fused != 0);
+}
+
+int bfp8_set_weight_prefetch(int enabled) {
+  return g_weight_prefetch.exchange(enabled ? 1 : 0);
+}
+
 int bfp8_plan_shape(const bfp8_gemm_problem* p, bfp8_plan plan, int* tiles, int* k_tiles) {
   if (!p || !config_ok(plan.config)) return fail(BFP8_EINVAL, "bad config id");
   const Derived d = derive(*p, plan);
   if (tiles) *tiles = d.tiles;
   if (k_tiles) *k_tiles = d.k_tiles;
+  return BFP8_OK;
+}
+
+// Weight-streaming configurations hold all tokens in one tile.
+int check_tokens(const bfp8_gemm_problem& p, const bfp8_plan& plan) {
+  const ConfigEntry& e = kConfigs[plan.config];
+  if (e.stream && p.M > e.max_m)
+    return fail(BFP8_EINVAL, std::string(e.name) + " handles at most " + std::to_string(e.max_m) + " tokens");
   return BFP8_OK;
 }
 
@@ -545,6 +699,7 @@ int64_t bfp8_workspace_bytes(const bfp8_gemm_problem* p, bfp8_plan plan) {
   if (!p || !config_ok(plan.config)) return fail(BFP8_EINVAL, "bad config id");
   if (int r = check_schedule(plan)) return r;
   if (p->M <= 0) return 0;
+  if (int r = check_tokens(*p, plan)) return r;
   const bool front = plan.fused && !quantizes_in_kernel(*p, plan);
   return (front ? fused_front_bytes(*p) : 0) + splitk_bytes(*p, plan);
 }
@@ -553,6 +708,7 @@ int bfp8_counters_needed(const bfp8_gemm_problem* p, bfp8_plan plan) {
   if (!p || !config_ok(plan.config)) return fail(BFP8_EINVAL, "bad config id");
   if (int r = check_schedule(plan)) return r;
   if (p->M <= 0) return 0;
+  if (int r = check_tokens(*p, plan)) return r;
   const Derived d = derive(*p, plan);
   return d.splits == 1 ? 0 : d.tiles * (kConfigs[plan.config].bm / 128);
 }
@@ -592,6 +748,102 @@ int check_tp(const bfp8_gemm_problem& p, const bfp8_tp_group& tp) {
   return BFP8_OK;
 }
 
+// Shared-memory layout of a weight-streaming launch: the ring of stages
+// (`group` K blocks each: weight tiles, e4m3 activation tiles and, when the
+// kernel quantizes, bf16 activation tiles), then the per-position token and
+// weight scales and the barriers.  Preferred: at most 112 KB, so that two
+// CTAs fit on an SM (the next call's CTAs start beside this call's); stages
+// of 2 K blocks x 3 when they fit, else smaller.  Problems whose scale
+// arrays do not allow that use the whole of shared memory.
+struct StreamLayout {
+  int stages, group, smem;
+  uint32_t stage_bytes, off_sa, off_sb, off_bars;
+};
+
+constexpr int kStreamPairSmem = 112 * 1024;
+
+int stream_layout(int bn, bool quant, int M, const Derived& d, StreamLayout* out) {
+  const int64_t span = (d.sk_work + d.sk_grid - 1) / d.sk_grid;
+  const int acc = 256 / bn;  // StreamCfg::ACC_BUFS
+  auto a16 = [](int64_t x) { return (x + 15) & ~int64_t(15); };
+  auto fits = [&](int s, int group, int limit, StreamLayout* o) {
+    // (1024-byte multiples: every stage's tiles keep the 128-byte swizzle's alignment)
+    const int64_t stage = (int64_t(group) * (16384 + bn * 128 + (quant ? std::min(M, bn) * 256 : 0)) + 1023) & ~int64_t(1023);
+    const int64_t off_sa = int64_t(s) * stage;
+    const int64_t off_sb = off_sa + a16(span * bn * 4);
+    const int64_t off_bars = off_sb + a16(span * 4);
+    const int64_t end = off_bars + (4 * s + 2 * acc + 1) * 8 + 16;
+    if (1024 + end > limit) return false;
+    *o = {s, group, int(1024 + end), uint32_t(stage), uint32_t(off_sa), uint32_t(off_sb), uint32_t(off_bars)};
+    return true;
+  };
+  const int pair[][2] = {{3, 2}, {2, 2}, {3, 1}, {2, 1}};  // {stages, K blocks per stage}, two CTAs per SM
+  for (const auto& t : pair)
+    if (fits(t[0], t[1], kStreamPairSmem, out)) return BFP8_OK;
+  const int alone[][2] = {{3, 4}, {2, 4}, {4, 2}, {3, 2}, {2, 2}, {3, 1}, {2, 1}};
+  for (const auto& t : alone)
+    if (fits(t[0], t[1], kMaxSmem, out)) return BFP8_OK;
+  return fail(BFP8_EINVAL, "this problem's per-CTA scale arrays do not fit a weight-streaming configuration's "
+                           "shared memory (use more CTAs or another configuration)");
+}
+
+int launch_stream(const bfp8_gemm_problem& p, const void* x_bf16, const bfp8_plan& plan, const Derived& d,
+                  bool in_kernel, uint8_t* ws, int* counters, int dev, cudaStream_t stream) {
+  const ConfigEntry& e = kConfigs[plan.config];
+  if (d.sk_work >= (int64_t(1) << 31)) return fail(BFP8_EINVAL, "too many weight tiles x K blocks for " + std::string(e.name));
+  StreamLayout lay;
+  if (int r = stream_layout(e.bn, in_kernel, p.M, d, &lay)) return r;
+  StreamParams sp;
+  std::memset(&sp, 0, sizeof(sp));
+  if (int r = make_map(&sp.map_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.b, uint64_t(p.K), uint64_t(p.N),
+                       uint64_t(p.ldb), 128, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+    return r;
+  if (in_kernel) {
+    // bf16 activations: [BN rows x 128 values] boxes, quantized in the kernel
+    const int rows = std::min(p.M, e.bn);
+    if (int r = make_map(&sp.map_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x_bf16, uint64_t(p.K), uint64_t(p.M),
+                         uint64_t(p.lda) * 2, 128, uint32_t(rows), CU_TENSOR_MAP_SWIZZLE_NONE))
+      return r;
+    sp.eps = p.eps;
+    sp.x_bytes = uint32_t(rows) * 256u;
+  } else {
+    if (int r = make_map(&sp.map_x, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.a, uint64_t(p.K), uint64_t(p.M),
+                         uint64_t(p.lda), 128, uint32_t(e.bn), CU_TENSOR_MAP_SWIZZLE_128B))
+      return r;
+    sp.sa = p.sa;
+    sp.sa_m = p.sa_m;
+    sp.sa_k = p.sa_k;
+  }
+  sp.sb = p.sb;
+  sp.sb_n = p.sb_n;
+  sp.sb_k = p.sb_k;
+  sp.c = static_cast<__nv_bfloat16*>(p.c);
+  sp.ldc = p.ldc;
+  sp.workspace = reinterpret_cast<float*>(ws);
+  sp.counters = counters;
+  sp.M = p.M;
+  sp.N = p.N;
+  sp.K = p.K;
+  sp.tiles = d.tiles;
+  sp.k_tiles = d.k_tiles;
+  sp.max_pieces = d.splits;
+  sp.work = int(d.sk_work);
+  sp.work_q = int(d.sk_work / d.sk_grid);
+  sp.work_r = int(d.sk_work % d.sk_grid);
+  sp.stages = lay.stages;
+  sp.group = lay.group;
+  sp.early = g_weight_prefetch.load(std::memory_order_relaxed) ? lay.stages : 0;
+  sp.stage_bytes = lay.stage_bytes;
+  sp.off_sa = lay.off_sa;
+  sp.off_sb = lay.off_sb;
+  sp.off_bars = lay.off_bars;
+  if (int r = ensure_smem_attr(plan.config, dev, in_kernel)) return r;
+  (in_kernel ? e.launch_stream_q : e.launch_stream)(sp, d.sk_grid, lay.smem, true, stream);
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) return cuda_fail(err, "weight-streaming GEMM launch");
+  return BFP8_OK;
+}
+
 int launch_gemm_impl(const bfp8_gemm_problem* pp, bfp8_plan plan, float* workspace, int* counters,
                      const bfp8_tp_group* tp, void* stream_) {
   if (!pp) return fail(BFP8_EINVAL, "null problem");
@@ -609,6 +861,9 @@ int launch_gemm_impl(const bfp8_gemm_problem* pp, bfp8_plan plan, float* workspa
 
   const Derived d = derive(p, plan);
   const bool in_kernel = quantizes_in_kernel(p, plan);
+  if (int r = check_tokens(p, plan)) return r;
+  if (tp && kConfigs[plan.config].stream)
+    return fail(BFP8_EINVAL, std::string(kConfigs[plan.config].name) + " has no row-parallel variant");
   if (((fused && !in_kernel) || d.splits > 1) && !workspace) return fail(BFP8_EINVAL, "workspace required");
   if (d.splits > 1 && !counters) return fail(BFP8_EINVAL, "split-K counters required");
 
@@ -631,6 +886,7 @@ int launch_gemm_impl(const bfp8_gemm_problem* pp, bfp8_plan plan, float* workspa
   }
 
   const ConfigEntry& e = kConfigs[plan.config];
+  if (e.stream) return launch_stream(p, x_bf16, plan, d, in_kernel, ws, counters, dev, stream);
   GemmParams gp;
   std::memset(&gp, 0, sizeof(gp));
   if (in_kernel) {
@@ -690,7 +946,7 @@ int launch_gemm_impl(const bfp8_gemm_problem* pp, bfp8_plan plan, float* workspa
   const int64_t a_bytes = int64_t(d.tiles_r) * e.bm * p.K;
   gp.group_r = e.swap || a_bytes <= (int64_t(48) << 20) ? d.tiles_r : 1024 / e.bm;
   gp.stream_b = (e.swap || p.M <= 128) ? 1 : 0;  // weights read once: evict them first
-  gp.pdl = fused && !in_kernel ? 1 : 0;
+  gp.pdl = g_weight_prefetch.load(std::memory_order_relaxed) ? 1 : 0;  // early weight tiles
   if (tp) {
     gp.tp_world = tp->world;
     gp.tp_rank = tp->rank;
@@ -726,6 +982,8 @@ int bfp8_launch_gemm(const bfp8_gemm_problem* p, bfp8_plan plan, float* workspac
 
 int bfp8_tp_tiles(const bfp8_gemm_problem* p, bfp8_plan plan) {
   if (!p || !config_ok(plan.config)) return fail(BFP8_EINVAL, "bad config id");
+  if (kConfigs[plan.config].stream)
+    return fail(BFP8_EINVAL, std::string(kConfigs[plan.config].name) + " has no row-parallel variant");
   if (int r = check_schedule(plan)) return r;
   if (p->M <= 0) return 0;
   const Derived d = derive(*p, plan);
@@ -920,4 +1178,23 @@ extern "C" int bfp8_probe_block(const void* a, const void* b, float* d, void* st
       static_cast<const uint8_t*>(a), static_cast<const uint8_t*>(b), d);
   err = cudaGetLastError();
   return err == cudaSuccess ? BFP8_OK : cuda_fail(err, "probe launch");
+}
+
+extern "C" int bfp8_probe_quantizer(float eps, unsigned long long* mismatches, unsigned long long* first) {
+  if (!mismatches || !(eps > 0.f)) return bfp8::fail(BFP8_EINVAL, "probe arguments");
+  unsigned long long* d = nullptr;
+  cudaError_t err = cudaMalloc(&d, 2 * sizeof(unsigned long long));
+  if (err != cudaSuccess) return bfp8::cuda_fail(err, "cudaMalloc (probe)");
+  err = cudaMemset(d, 0, 2 * sizeof(unsigned long long));
+  if (err == cudaSuccess) {
+    bfp8::probe_quant_kernel<<<0x7F80, 256>>>(eps, d);
+    err = cudaGetLastError();
+  }
+  unsigned long long h[2] = {0, 0};
+  if (err == cudaSuccess) err = cudaMemcpy(h, d, sizeof(h), cudaMemcpyDeviceToHost);
+  cudaFree(d);
+  if (err != cudaSuccess) return bfp8::cuda_fail(err, "probe launch");
+  *mismatches = h[0];
+  if (first) *first = h[1];
+  return BFP8_OK;
 }

@@ -79,6 +79,7 @@
 #include <cstdint>
 
 #include "ptx.cuh"
+#include "quant_math.cuh"
 
 namespace bfp8 {
 
@@ -361,29 +362,10 @@ __device__ __forceinline__ void quantize_unit(const GemmParams& p, const UnitCoo
     for (int b = 0; b < QB; ++b) {
       const int gi = g0 + half + b * HALVES;
       const int kl = gi / rows, row = gi % rows;
-      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&cur[b]);
-      float f[8];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 t = __bfloat1622float2(h[e]);
-        f[2 * e] = t.x;
-        f[2 * e + 1] = t.y;
-      }
-      float amax = p.eps;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(f[e]));
-#pragma unroll
-      for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      const GroupQuant gq = quantize_group(cur[b], p.eps);  // all 32 lanes (shuffles)
       if (gi < groups) {
-        const float scale = amax / 448.f;
-        uint32_t packed[2] = {0u, 0u};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 q = make_float2(fminf(fmaxf(f[2 * e] / scale, -448.f), 448.f),
-                                       fminf(fmaxf(f[2 * e + 1] / scale, -448.f), 448.f));
-          const uint32_t pair = __nv_cvt_float2_to_fp8x2(q, __NV_SATFINITE, __NV_E4M3);
-          packed[e >> 1] |= pair << (16 * (e & 1));
-        }
+        const float scale = gq.scale;
+        const uint32_t packed[2] = {gq.codes.x, gq.codes.y};
         // 8 codes of chunk lane16 of token row `row`: 16-byte unit lane16 / 2
         // of the row, XOR-swizzled with the row inside its 8-row group.
         const uint32_t unit16 = uint32_t(lane16 >> 1) ^ uint32_t(row & 7);
@@ -411,6 +393,10 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) gemm_kernel(const __grid_cons
   constexpr bool SWAP = Cfg::SWAP, FUSE = Cfg::FUSE, PAIR = Cfg::PAIR;
   constexpr int CG = Cfg::CG;
   constexpr int PF = 4;  // scale prefetch distance in K blocks
+
+  // The next kernel of the stream may launch now (programmatic dependent
+  // launch); it waits for this grid's completion before it uses our output.
+  griddep_launch_dependents();
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);

@@ -10,6 +10,7 @@
 #include <cstdint>
 
 #include "ptx.cuh"
+#include "quant_math.cuh"
 
 namespace bfp8 {
 
@@ -133,6 +134,41 @@ __global__ void __launch_bounds__(256) probe_read_kernel(const uint4* __restrict
     acc ^= a.x ^ a.y ^ a.z ^ a.w;
   }
   sink[blockIdx.x * blockDim.x + threadIdx.x] = acc;
+}
+
+// Exhaustive check of the quantizer's fast path (group_codes_fast) against
+// the reference's sequence (group_codes_exact) on its whole input domain:
+// block a uses amax = max(eps, the bf16 magnitude with bits a), a in
+// [0, 0x7F80) (a = 0 gives amax = eps), and its threads cover all 65536 bf16
+// patterns x, 8 at a time; x that is not finite or above amax cannot occur
+// in a group with that amax and is skipped.  out[0] counts the codes that
+// differ, out[1] holds the first mismatch as (a << 32) | x + 1.
+__global__ void __launch_bounds__(256) probe_quant_kernel(float eps, unsigned long long* out) {
+  const uint32_t a = blockIdx.x;
+  const float amax = fmaxf(eps, __uint_as_float(a << 16));
+  const float scale = amax / 448.f;
+  const float r = __frcp_rn(scale);
+  unsigned long long bad = 0;
+  for (uint32_t x0 = threadIdx.x * 8u; x0 < 65536u; x0 += blockDim.x * 8u) {
+    const uint4 v = make_uint4(x0 | ((x0 + 1u) << 16), (x0 + 2u) | ((x0 + 3u) << 16), (x0 + 4u) | ((x0 + 5u) << 16),
+                               (x0 + 6u) | ((x0 + 7u) << 16));
+    float f[8];
+    bf16x8_to_float(v, f);
+    const uint2 fast = group_codes_fast(v, scale, r);
+    const uint2 exact = group_codes_exact(f, scale);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const uint32_t x = x0 + uint32_t(e);
+      const bool valid = (x & 0x7FFFu) < 0x7F80u && fabsf(f[e]) <= amax;
+      const uint32_t cf = ((e < 4 ? fast.x : fast.y) >> (8 * (e & 3))) & 0xFFu;
+      const uint32_t ce = ((e < 4 ? exact.x : exact.y) >> (8 * (e & 3))) & 0xFFu;
+      if (valid && cf != ce) {
+        ++bad;
+        atomicCAS(out + 1, 0ull, (static_cast<unsigned long long>(a) << 32) | (x + 1u));
+      }
+    }
+  }
+  if (bad) atomicAdd(out, bad);
 }
 
 }  // namespace bfp8

@@ -19,6 +19,8 @@
 
 #include <cstdint>
 
+#include "quant_math.cuh"
+
 namespace bfp8 {
 
 struct QuantParams {
@@ -40,59 +42,48 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_kernel(const QuantPara
   // A GEMM launched behind this kernel with programmatic dependent launch may
   // start now: it only reads our output after griddepcontrol.wait.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // This kernel may itself start before the previous kernel of the stream
+  // has finished: x may be its output, and q and s may still be read by it.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int lane16 = threadIdx.x & 15;
   const int half = threadIdx.x >> 4;  // 0 .. 15: the row within the task
   const int row_blocks = (p.M + kQuantRows - 1) / kQuantRows;
   const int group_blocks = (p.kb + kQuantGroups - 1) / kQuantGroups;
-  const int64_t tasks = int64_t(row_blocks) * group_blocks;
-#pragma unroll 1
-  for (int64_t t = blockIdx.x; t < tasks; t += gridDim.x) {
-    // Row blocks vary fastest: neighbouring CTAs share a group range, so
-    // their scale stores land in the same lines.
-    const int rb = int(t % row_blocks), gb = int(t / row_blocks);
+  const int tasks = row_blocks * group_blocks;  // < 2^31 (checked by the host)
+  // Task t: rows rb * 16 .. + 15 (one per half-warp), groups gb * 4 .. + 3.
+  // Row blocks vary fastest: neighbouring CTAs share a group range, so their
+  // scale stores land in the same lines.  The loads of a CTA's next task go
+  // out before the current one is converted.
+  auto load = [&](int t, uint4 (&v)[kQuantGroups]) {
+    const int gb = t / row_blocks, rb = t - gb * row_blocks;
     const int row = rb * kQuantRows + half;
-    const bool row_ok = row < p.M;  // uniform per half-warp
-    const __nv_bfloat16* xr = p.x + int64_t(row_ok ? row : 0) * p.ldx;
-
-    uint4 v[kQuantGroups];
 #pragma unroll
     for (int j = 0; j < kQuantGroups; ++j) {
       const int col = (gb * kQuantGroups + j) * 128 + lane16 * 8;
       v[j] = make_uint4(0u, 0u, 0u, 0u);  // zeros leave the amax alone
-      if (row_ok && col < p.K) v[j] = __ldcs(reinterpret_cast<const uint4*>(xr + col));
+      if (row < p.M && col < p.K) v[j] = __ldcs(reinterpret_cast<const uint4*>(p.x + int64_t(row) * p.ldx + col));
     }
+  };
+  uint4 cur[kQuantGroups], nxt[kQuantGroups];
+  int t = blockIdx.x;
+  if (t < tasks) load(t, cur);
+#pragma unroll 1
+  for (; t < tasks; t += gridDim.x) {
+    if (t + int(gridDim.x) < tasks) load(t + gridDim.x, nxt);
+    const int gb = t / row_blocks, rb = t - gb * row_blocks;
+    const int row = rb * kQuantRows + half;
+    const bool row_ok = row < p.M;  // uniform per half-warp
+    uint8_t* qrow = p.q + int64_t(row) * p.ldq;
 #pragma unroll
     for (int j = 0; j < kQuantGroups; ++j) {
       const int g = gb * kQuantGroups + j;
       const int col = g * 128 + lane16 * 8;
-      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v[j]);
-      float f[8];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 u = __bfloat1622float2(h[e]);
-        f[2 * e] = u.x;
-        f[2 * e + 1] = u.y;
-      }
-      float amax = p.eps;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(f[e]));
-      // All 32 lanes take part; the xor offsets stay inside each half-warp.
-#pragma unroll
-      for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-      const float scale = amax / 448.f;
-      if (row_ok && col < p.K) {
-        uint32_t packed[2] = {0u, 0u};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 u = make_float2(fminf(fmaxf(f[2 * e] / scale, -448.f), 448.f),
-                                       fminf(fmaxf(f[2 * e + 1] / scale, -448.f), 448.f));
-          const uint32_t pair = __nv_cvt_float2_to_fp8x2(u, __NV_SATFINITE, __NV_E4M3);
-          packed[e >> 1] |= pair << (16 * (e & 1));
-        }
-        *reinterpret_cast<uint2*>(p.q + int64_t(row) * p.ldq + col) = make_uint2(packed[0], packed[1]);
-      }
-      if (row_ok && g < p.kb && lane16 == 0) p.s[int64_t(row) * p.s_m + int64_t(g) * p.s_k] = scale;
+      const GroupQuant gq = quantize_group(cur[j], p.eps);  // all 32 lanes (shuffles)
+      if (row_ok && col < p.K) *reinterpret_cast<uint2*>(qrow + col) = gq.codes;
+      if (row_ok && g < p.kb && lane16 == 0) p.s[int64_t(row) * p.s_m + int64_t(g) * p.s_k] = gq.scale;
     }
+#pragma unroll
+    for (int j = 0; j < kQuantGroups; ++j) cur[j] = nxt[j];
   }
 }
 

@@ -122,6 +122,8 @@ class RowParallelGroup:
         part, tiles = 16, 1
         for cfg in range(self._lib.bfp8_num_configs()):
             plan = _native.Plan(cfg, 1, 0)
+            if self._lib.bfp8_tp_tiles(ctypes.byref(probe), plan) < 0:
+                continue  # no row-parallel variant (the weight-streaming configurations)
             part = max(part, capi.tp_partial_bytes(probe, plan, self.world))
             tiles = max(tiles, capi.tp_tiles(probe, plan))
         sizes = (part, 8 * (2 + tiles), 2 * max_m * n)
@@ -173,7 +175,7 @@ class RowParallelGroup:
         x = x.contiguous()
         fused = bool(self._lib.bfp8_prefers_fused(m, n, self.k_plan))
         sms = torch.cuda.get_device_properties(self.device).multi_processor_count
-        plan = capi.choose_plan(m, n, self.k_plan, sms, fused)
+        plan = self._lib.bfp8_choose_tp_plan(m, n, self.k_plan, sms, int(fused))
         if fused:
             p = capi.problem(x, None, b_q, b_scales, out)
         else:

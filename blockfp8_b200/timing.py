@@ -22,6 +22,40 @@ def copies_for(weight_bytes: int, factor: float = 2.5) -> int:
     return max(2, math.ceil(factor * L2_BYTES / max(1, weight_bytes)))
 
 
+def rotating_graph_stats(call, copies: int, calls: int = 64, replays: int = 7, warm_replays: int = 2) -> dict:
+    """Per-call device microseconds of one graph of `calls` calls (cycling
+    i over range(copies)), replayed `replays` times: median and
+    interquartile range over the replays."""
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        for i in range(copies):
+            call(i)  # first launches outside capture (per-device setup)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for j in range(calls):
+                call(j % copies)
+    torch.cuda.current_stream().wait_stream(stream)
+    for _ in range(warm_replays):
+        graph.replay()
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(replays)]
+    for start, end in events:
+        start.record()
+        graph.replay()
+        end.record()
+    torch.cuda.synchronize()
+    us = sorted(s.elapsed_time(e) * 1e3 / calls for s, e in events)
+    del graph
+
+    def quantile(q):
+        x = q * (len(us) - 1)
+        lo = int(math.floor(x))
+        hi = min(lo + 1, len(us) - 1)
+        return us[lo] + (us[hi] - us[lo]) * (x - lo)
+
+    return {"median": quantile(0.5), "q1": quantile(0.25), "q3": quantile(0.75), "replays": replays}
+
+
 def rotating_graph_us(call, copies: int, calls: int = 64, warm_replays: int = 2) -> float:
     """Mean device microseconds per call(i) over one graph of `calls` calls,
     cycling i over range(copies)."""

@@ -98,6 +98,12 @@ bfp8_plan bfp8_choose_fused_plan(int M, int N, int K, int num_sms);
 /* (choose_fused_plan's plan.fused is the faster of the two fused modes for
  * the shape, as tuned on a B200.) */
 
+/* The built-in plan among the configurations that have a row-parallel twin
+ * (bfp8_launch_gemm_tp); fused != 0 asks for BFP8_FUSED_QUANT_KERNEL.  The
+ * weight-streaming configurations ("w128d...") that bfp8_choose_plan picks
+ * for decode batches have none.  No counterpart in the reference. */
+bfp8_plan bfp8_choose_tp_plan(int M, int N, int K, int num_sms, int fused);
+
 /* Whether linear runs this shape through the fused path; replaces
  * prefers_fused (csrc/blockfp8.h:47-50).  Returns 0 or 1. */
 int bfp8_prefers_fused(int M, int N, int K);
@@ -201,6 +207,19 @@ int bfp8_tp_open(const void* handle, void** ptr);
 int bfp8_tp_close(void* ptr);
 int bfp8_tp_free(void* ptr);
 
+/* Programmatic dependent launch.  Every GEMM and quantizer launch may start
+ * while the previous kernel of its stream is still running: it waits
+ * (griddepcontrol.wait) before reading activations or activation scales and
+ * before writing anything, and it lets the next kernel start early.  With
+ * weight prefetch on (the default) the GEMMs also request their first weight
+ * tiles and read weight scales before that wait, so that behind another
+ * GEMM the weight stream never stops.  Weights and weight scales must
+ * therefore not be written by the kernel that immediately precedes the call
+ * in its stream (model weights are written once, long before).  Turn it off
+ * for code that writes weights right before using them.  Process-wide;
+ * returns the previous setting.  No counterpart in the reference. */
+int bfp8_set_weight_prefetch(int enabled);
+
 /* Launch the activation quantizer; replaces launch_quantize
  * (csrc/blockfp8.h:76).  Returns BFP8_OK, BFP8_EINVAL or BFP8_ECUDA. */
 int bfp8_launch_quantize(const bfp8_quant_problem* p, void* stream);
@@ -231,6 +250,13 @@ int bfp8_probe_hbm_read(const void* buf, int64_t bytes, int reps, double* gbs);
  * aligned) -> d [128 x 32] fp32 = four K = 32 tcgen05 MMAs, unscaled, before
  * any rounding of the GEMM's own.  For measuring the MMA's accumulation. */
 int bfp8_probe_block(const void* a, const void* b, float* d, void* stream);
+/* Exhaustive check of the activation quantizer's arithmetic: the fast path
+ * the kernels use (reciprocal times x with one correction step) against the
+ * reference's sequence (one IEEE division per value), on every pair of a
+ * group amax (eps or any finite bf16 magnitude) and a bf16 value up to it.
+ * *mismatches = codes that differ; *first = (amax bits << 32) | (x bits + 1)
+ * of the first one, 0 if none.  Synchronous; allocates a few bytes. */
+int bfp8_probe_quantizer(float eps, unsigned long long* mismatches, unsigned long long* first);
 
 #ifdef __cplusplus
 }

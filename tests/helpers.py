@@ -1,5 +1,7 @@
 """Shared test helpers: seeded operands and comparisons against the CPU oracle."""
 
+import re
+
 import numpy as np
 import torch
 
@@ -94,3 +96,18 @@ def assert_close(c: torch.Tensor, ref: np.ndarray, rtol=RTOL, atol_rel_max=ATOL_
     assert np.all(np.isfinite(got)), "non-finite output"
     assert worst <= 1.0, f"error exceeds the tolerance by {worst:.3g}x"
     return worst
+
+
+def token_limit(name: str):
+    """Most tokens (M) a weight-streaming configuration ("w128d<BN>")
+    handles; None for the tile configurations, which take any M."""
+    m = re.fullmatch(r"w128d(\d+)", name)
+    return int(m.group(1)) if m else None
+
+
+def config_geometry(name: str):
+    """(MMA rows of a tile, tile width BN, swapped order) of a configuration
+    name: "m<BM>n<BN>..." (activation rows x weight rows), "w128t<BN>..." and
+    "w128d<BN>" (weight rows x tokens)."""
+    m = re.match(r"([mw])(\d+)[ntd](\d+)", name)
+    return int(m.group(2)), int(m.group(3)), m.group(1) == "w"

@@ -13,6 +13,7 @@ import torch
 
 import blockfp8
 import blockfp8_b200
+from helpers import config_geometry, token_limit
 from blockfp8_b200 import _native
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -143,7 +144,8 @@ def test_c_abi_answers_without_a_gpu():
     for m, nn, k in [(1, 6144, 4096), (16, 24576, 4096), (256, 6144, 4096), (8192, 24576, 4096),
                      (3000, 4096, 12288), (33, 264, 272)]:
         plan = lib.bfp8_choose_plan(m, nn, k, 148)
-        assert 0 <= plan.config < n and plan.splits >= 1 and plan.fused == 0
+        assert 0 <= plan.config < n and plan.splits != 0 and plan.fused == 0
+        assert plan.splits >= 1 or names[plan.config].startswith("w")  # stream-K: the decode configurations
         fplan = lib.bfp8_choose_fused_plan(m, nn, k, 148)
         assert fplan.fused in (1, 2)
         if fplan.fused == 1:  # quantization kernel + the GEMM's own plan: same bits as unfused
@@ -154,8 +156,10 @@ def test_c_abi_answers_without_a_gpu():
         assert kt.value == -(-k // 128)
         ws = lib.bfp8_workspace_bytes(ctypes.byref(p), plan)
         cnt = lib.bfp8_counters_needed(ctypes.byref(p), plan)
-        splits = -(-kt.value // -(-kt.value // min(plan.splits, kt.value)))
-        assert (ws == 0) == (splits == 1) and (cnt == 0) == (splits == 1)
+        if plan.splits > 0 and token_limit(names[plan.config]) is None:
+            splits = -(-kt.value // -(-kt.value // min(plan.splits, kt.value)))
+            assert (ws == 0) == (splits == 1) and (cnt == 0) == (splits == 1)
+        assert ws >= 0 and cnt >= 0 and (ws == 0) == (cnt == 0)
         # quantization kernel first: q and s live in the front of the workspace
         q_plan = _native.Plan(plan.config, plan.splits, 1)
         assert lib.bfp8_workspace_bytes(ctypes.byref(p), q_plan) >= m * k + ws
@@ -166,9 +170,17 @@ def test_c_abi_answers_without_a_gpu():
             for splits in (1, 2, 4, 8):
                 in_plan, q_plan = _native.Plan(config, splits, 2), _native.Plan(config, splits, 1)
                 p_plan = _native.Plan(config, splits, 0)
-                bn = int(re.match(r"[mw]\d+[nt](\d+)", names[config]).group(1))
+                _, bn, _ = config_geometry(names[config])
                 per = -(-kt.value // min(splits, kt.value))
-                fits = names[config].startswith("w") and per * bn * 128 <= 65536
+                lim = token_limit(names[config])
+                if lim is not None:  # weight streaming: any K range quantizes in the kernel
+                    fits = True
+                    if m > lim:  # refused: more tokens than the tile holds
+                        assert lib.bfp8_workspace_bytes(ctypes.byref(p), in_plan) < 0
+                        assert "tokens" in lib.bfp8_last_error().decode()
+                        continue
+                else:
+                    fits = names[config].startswith("w") and per * bn * 128 <= 65536
                 expect = p_plan if fits else q_plan
                 assert lib.bfp8_workspace_bytes(ctypes.byref(p), in_plan) == \
                     lib.bfp8_workspace_bytes(ctypes.byref(p), expect)
@@ -201,7 +213,25 @@ def test_stream_k_plan_sizes(m, n, k, ctas):
     names = [lib.bfp8_config_name(i).decode() for i in range(lib.bfp8_num_configs())]
     p = _native.GemmProblem(M=m, N=n, K=k)
     for config, name in enumerate(names):
-        bm, bn = (int(v) for v in re.match(r"[mw](\d+)[nt](\d+)", name).groups())
+        bm, bn, _ = config_geometry(name)
+        lim = token_limit(name)
+        if lim is not None:
+            # weight streaming: the tiles are the weight rows only (all
+            # tokens in one tile); parts are [128 rows][M rounded up to 4] fp32
+            plan = _native.Plan(config, -ctas, 0)
+            if m > lim:
+                assert lib.bfp8_workspace_bytes(ctypes.byref(p), plan) < 0
+                continue
+            tiles = -(-n // 128)
+            parts, _ = _stream_k_parts(tiles, -(-k // 128), ctas)
+            most = max(parts)
+            expect_ws = 0 if most == 1 else most * tiles * 128 * ((m + 3) & ~3) * 4
+            assert lib.bfp8_workspace_bytes(ctypes.byref(p), plan) == expect_ws
+            assert lib.bfp8_counters_needed(ctypes.byref(p), plan) == (0 if most == 1 else tiles)
+            # quantization in the kernel needs no front; the kernel + GEMM mode does
+            assert lib.bfp8_workspace_bytes(ctypes.byref(p), _native.Plan(config, -ctas, 2)) == expect_ws
+            assert lib.bfp8_workspace_bytes(ctypes.byref(p), _native.Plan(config, -ctas, 1)) > expect_ws
+            continue
         if bm == 256:  # CTA pairs: no stream-K schedule, refused with a reason
             assert lib.bfp8_workspace_bytes(ctypes.byref(p), _native.Plan(config, -ctas, 0)) < 0
             assert "stream-K" in lib.bfp8_last_error().decode()
@@ -279,7 +309,11 @@ def test_row_parallel_sizes_and_argument_checks():
     for m, n in [(1, 4096), (300, 520), (8192, 24576)]:
         p = _native.GemmProblem(M=m, N=n, K=2048)
         for config, name in enumerate(names):
-            bm, bn = (int(v) for v in re.match(r"[mw](\d+)[nt](\d+)", name).groups())
+            bm, bn, _ = config_geometry(name)
+            if token_limit(name) is not None:  # weight streaming: no row-parallel variant
+                assert lib.bfp8_tp_tiles(ctypes.byref(p), _native.Plan(config, 1, 0)) < 0
+                assert "row-parallel" in lib.bfp8_last_error().decode()
+                continue
             rows, cols = (n, m) if name.startswith("w") else (m, n)
             tiles = -(-rows // bm) * -(-cols // bn) * (bm // 128)
             plan = _native.Plan(config, 1, 0)
@@ -321,7 +355,11 @@ def test_plan_table_rows_are_layer_or_shard_shapes():
     assert rows and all((n, k) in shapes for n, k, _ in rows)
     for (n, k, m), (config, splits) in rows.items():
         assert 0 <= config < lib.bfp8_num_configs() and splits != 0
-        assert lib.bfp8_choose_plan(m, n, k, 148).config == config or m >= 256  # exact rows are returned as tuned
+        # exact rows are returned as tuned; up to 32 tokens the planner takes the
+        # weight-streaming configurations, and the tuned rows serve the
+        # row-parallel kernel (whose configurations are the tile ones)
+        chosen = lib.bfp8_choose_tp_plan(m, n, k, 148, 0) if m <= 32 else lib.bfp8_choose_plan(m, n, k, 148)
+        assert chosen.config == config or m >= 256
 
 
 def test_untabulated_decode_shapes_take_swapped_configurations():

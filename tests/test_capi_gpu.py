@@ -13,7 +13,7 @@ import torch
 
 from blockfp8_b200 import _native, capi
 from helpers import (FP8, assert_close, assert_exact, bf16_activations, codes, f32,
-                     integer_operands, oracle_gemm, oracle_quant)
+                     integer_operands, oracle_gemm, oracle_quant, token_limit)
 from oracle import oracle as O
 
 pytestmark = [
@@ -36,7 +36,7 @@ def test_library_reports_itself():
     lib = _native.capi()
     assert lib.bfp8_abi_version() == 1
     assert lib.bfp8_num_configs() >= 1
-    assert capi.choose_plan(1, 6144, 4096, 148).splits >= 1
+    assert capi.choose_plan(1, 6144, 4096, 148).splits != 0  # decode: stream-K over the SMs
 
 
 @pytest.mark.parametrize("m", [1, 7, 33])
@@ -130,6 +130,8 @@ def test_both_fused_modes_equal_the_quantized_gemm(m, n, k, splits):
     for config in range(lib.bfp8_num_configs()):
         if splits < 0 and names[config].startswith("m256"):
             continue  # CTA pairs have no stream-K schedule
+        if (token_limit(names[config]) or m) < m:
+            continue  # more tokens than a weight-streaming tile holds
         expect = capi.gemm(q, s, b, sb, config=config, splits=splits)
         for mode in (1, 2):
             got = capi.gemm(x, None, b, sb, config=config, splits=splits, fused=mode)

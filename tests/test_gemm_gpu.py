@@ -14,7 +14,7 @@ import torch
 
 import blockfp8
 from helpers import (FP8, assert_close, assert_exact, bf16_activations, codes, f32,
-                     integer_operands, oracle_gemm, oracle_quant, realistic_operands)
+                     integer_operands, oracle_gemm, oracle_quant, realistic_operands, token_limit)
 from oracle import oracle as O
 
 pytestmark = [
@@ -42,6 +42,17 @@ def _pair(config):
     """Configurations on a CTA pair (256-row tiles, cta_group::2)."""
     return blockfp8.native_available() and blockfp8.configs()[config].startswith("m256")
 
+
+def _tokens(config, m):
+    """Skip a weight-streaming configuration for more tokens than it holds
+    (it refuses them; decode sizes are covered by the tests below)."""
+    lim = token_limit(blockfp8.configs()[config]) if blockfp8.native_available() else None
+    if lim is not None and m > lim:
+        pytest.skip(f"{blockfp8.configs()[config]} handles at most {lim} tokens")
+
+
+STREAM = [i for i, n in enumerate(blockfp8.configs()) if token_limit(n)] if blockfp8.native_available() else []
+
 SHAPES = [
     (1, 128, 128),
     (5, 256, 384),
@@ -57,6 +68,7 @@ SHAPES = [
 @pytest.mark.parametrize("config", CONFIGS)
 @pytest.mark.parametrize("shape", SHAPES)
 def test_exact_integer_case_all_configs(config, shape):
+    _tokens(config, shape[0])
     a, sa, b, sb = integer_operands(*shape, seed=sum(shape) % 1000)
     c = blockfp8.gemm(a, sa, b, sb, config=config, split_k=1)
     assert_exact(c, oracle_gemm(a, sa, b, sb))
@@ -65,6 +77,7 @@ def test_exact_integer_case_all_configs(config, shape):
 @pytest.mark.parametrize("config", CONFIGS)
 @pytest.mark.parametrize("splits", [2, 3, 7])
 def test_exact_integer_case_split_k(config, splits):
+    _tokens(config, 37)
     a, sa, b, sb = integer_operands(37, 392, 2048 + 16, seed=splits)
     c = blockfp8.gemm(a, sa, b, sb, config=config, split_k=splits)
     assert_exact(c, oracle_gemm(a, sa, b, sb))
@@ -79,6 +92,7 @@ def test_exact_integer_case_stream_k(config, shape, ctas):
     into several parts (ragged, across tile boundaries) sum them in K order."""
     if _pair(config):
         pytest.skip("CTA-pair configurations have no stream-K schedule")
+    _tokens(config, shape[0])
     a, sa, b, sb = integer_operands(*shape, seed=ctas % 97)
     c = blockfp8.gemm(a, sa, b, sb, config=config, split_k=-ctas)
     assert_exact(c, oracle_gemm(a, sa, b, sb))
@@ -121,6 +135,7 @@ def test_realistic_within_tolerance_auto_plan(shape):
 def test_configs_agree_bitwise(config):
     # Every configuration computes each output the same way (four K = 32
     # MMAs per block from zero, one fmaf promotion per block, in order).
+    _tokens(config, 100)
     a, sa, b, sb = realistic_operands(100, 520, 1040, seed=21)
     assert torch.equal(blockfp8.gemm(a, sa, b, sb, config=config, split_k=1),
                        blockfp8.gemm(a, sa, b, sb, config=0, split_k=1))
@@ -168,6 +183,8 @@ def test_cancellation_across_blocks():
     sb2 = torch.cat([sb, sb], dim=1)
     big = oracle_gemm(a, sa, b, sb, absolute=True)
     for config in CONFIGS:
+        if (token_limit(blockfp8.configs()[config]) or 40) < 40:
+            continue
         c = blockfp8.gemm(a2, sa2, b2, sb2, config=config)
         ref = oracle_gemm(a2, sa2, b2, sb2)
         err = np.abs(c.double().cpu().numpy() - ref)
@@ -281,6 +298,7 @@ def _quantized(x: torch.Tensor, eps=1e-10):
 @pytest.mark.parametrize("ties", [False, True])
 def test_fused_equals_quantize_then_gemm(config, shape, ties):
     m, n, k = shape
+    _tokens(config, m)
     x = bf16_activations(m, k, seed=sum(shape) % 1000, ties=ties)
     b, sb = _weights(n, k, seed=1)
     a, sa = _quantized(x)
@@ -292,6 +310,7 @@ def test_fused_equals_quantize_then_gemm(config, shape, ties):
 @pytest.mark.parametrize("config", FUSED)
 @pytest.mark.parametrize("splits", [2, 3, 7])
 def test_fused_split_k(config, splits):
+    _tokens(config, 37)
     x = bf16_activations(37, 2048 + 16, seed=splits, ties=True)
     b, sb = _weights(392, 2048 + 16, seed=2)
     a, sa = _quantized(x)
@@ -308,6 +327,8 @@ def test_fused_zero_rows_outliers_and_eps():
     for eps in (1e-10, 1e-4):
         a, sa = _quantized(x, eps=eps)
         for config in FUSED:
+            if (token_limit(blockfp8.configs()[config]) or 20) < 20:
+                continue  # 20 tokens: more than a 16-token streaming tile holds
             c = blockfp8.gemm_bf16(x.to(DEV), b, sb, eps=eps, config=config, split_k=1)
             assert torch.equal(c, blockfp8.gemm(a, sa, b, sb, config=0, split_k=1))
             assert torch.all(c[3] == 0)
@@ -368,3 +389,54 @@ def test_ops_trace_under_torch_compile():
 
     out = torch.compile(f, fullgraph=True)(x, a, sa)
     assert torch.equal(out, f(x, a, sa))
+
+
+# ---- weight-streaming (decode) configurations -------------------------------------
+
+@pytest.mark.parametrize("config", STREAM)
+@pytest.mark.parametrize("m, n, k, splits", [(1, 6144, 4096, -148), (16, 4096, 12288, -148), (7, 520, 1040, -45),
+                                             (3, 1000, 1040, -1000), (16, 24576, 4096, -148), (5, 264, 272, 1),
+                                             (2, 392, 2064, 3), (13, 128, 128, -148)])
+def test_stream_exact_integer(config, m, n, k, splits):
+    """Exact-integer operands through every token tile, split count and
+    stream-K grid (tiles cut across CTAs, ragged K and N tails)."""
+    a, sa, b, sb = integer_operands(m, n, k, seed=m + n + (splits % 13))
+    c = blockfp8.gemm(a, sa, b, sb, config=config, split_k=splits)
+    assert_exact(c, oracle_gemm(a, sa, b, sb))
+
+
+@pytest.mark.parametrize("config", STREAM)
+def test_stream_one_split_agrees_bitwise_with_the_tile_kernels(config):
+    """One split: every tile's K blocks in order in one CTA, the same
+    promotion as every other configuration, so the same bits."""
+    a, sa, b, sb = realistic_operands(9, 520, 1040, seed=21)
+    assert torch.equal(blockfp8.gemm(a, sa, b, sb, config=config, split_k=1),
+                       blockfp8.gemm(a, sa, b, sb, config=0, split_k=1))
+
+
+@pytest.mark.parametrize("config", STREAM)
+@pytest.mark.parametrize("m", [1, 4, 16])
+def test_stream_fused_modes_bitwise_and_deterministic(config, m):
+    """bf16 in: the quantization kernel + streaming GEMM (mode 1) and the
+    streaming GEMM quantizing in its own warps (mode 2) both give
+    gemm(quantize(x))'s bits, call after call, within the tolerance of the
+    oracle."""
+    from blockfp8_b200 import capi
+    x = bf16_activations(m, 4096, seed=3 + m, ties=True).to(DEV)
+    b, sb = _weights(6144, 4096, seed=1)
+    q, s = capi.quantize(x)
+    expect = capi.gemm(q, s, b, sb, config=config, splits=-148)
+    for mode in (1, 2):
+        for _ in range(2):
+            assert torch.equal(capi.gemm(x, None, b, sb, config=config, splits=-148, fused=mode), expect), mode
+    assert_close(expect, oracle_gemm(q, s, b, sb))
+    from blockfp8_b200 import _native
+    assert _native.device_status(reset=True) == 0
+
+
+@pytest.mark.parametrize("config", STREAM)
+def test_stream_refuses_more_tokens_than_its_tile(config):
+    lim = token_limit(blockfp8.configs()[config])
+    a, sa, b, sb = realistic_operands(lim + 1, 256, 256, seed=2)
+    with pytest.raises(RuntimeError, match="tokens"):
+        blockfp8.gemm(a, sa, b, sb, config=config, split_k=-148)

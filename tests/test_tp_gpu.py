@@ -106,7 +106,7 @@ def test_realistic_operands_match_the_unsharded_product(world, shape):
     m, n, k = shape
     a, sa, b, sb = realistic_operands(m, n, k, seed=m)
     sms = torch.cuda.get_device_properties(0).multi_processor_count
-    plan = capi.choose_plan(m, n, sharding.block_slices(k, world, 0, 128)[1], sms)
+    plan = _native.capi().bfp8_choose_tp_plan(m, n, sharding.block_slices(k, world, 0, 128)[1], sms, 0)
     results, counters, tiles = emulate(world, a, sa, b, sb, plan)
     out = _check_group(results, counters, tiles, 2)
     ref = oracle_gemm(a, sa, b, sb)
