@@ -342,30 +342,45 @@ def weight_bytes(n, k):
     return n * k + 4 * (-(-n // 128)) * (-(-k // 128))
 
 
-def sweeps(dev, calls=48):
-    """Decode and prefill sweeps: per-call device time of blockfp8.linear (and
-    of the GEMM alone for prefill), from one CUDA graph of back-to-back calls
-    over weight copies that together exceed L2 (timing.rotating_graph_us)."""
+def sweeps(dev, calls=48, replays=7):
+    """Decode and prefill sweeps: per-call device time of blockfp8.linear and
+    of the GEMM alone (pre-quantized activations), from one CUDA graph of
+    back-to-back calls over weight copies that together exceed L2, replayed
+    `replays` times: median and interquartile range
+    (timing.rotating_graph_stats)."""
     import blockfp8_b200 as bf
     from blockfp8_b200 import timing
-    out = {"decode": {}, "prefill": {}}
+    out = {"decode": {}, "prefill": {}, "replays": replays,
+           "timing": "per-call device time in one CUDA graph of back-to-back calls over weight copies that "
+                     "together exceed L2 (cold weights); median [q1, q3] over the graph's replays"}
+
+    def stats(fn, copies, n_calls):
+        s = timing.rotating_graph_stats(fn, copies, n_calls, replays=replays)
+        return s["median"], [round(s["q1"], 2), round(s["q3"], 2)]
+
     for name, (n, k) in LAYERS.items():
         b0, sb0 = make_weights(n, k, dev, seed=1)
         copies = timing.copies_for(n * k)
         ws = [(b0, sb0)] + [(b0.clone(), sb0.clone()) for _ in range(copies - 1)]
         for m in DECODE_M:
             x = make_x(m, k, seed=m).to(dev)
-            us = timing.rotating_graph_us(lambda i: bf.linear(x, *ws[i]), copies, calls)
-            gbs = weight_bytes(n, k) / (us * 1e-6) / 1e9
-            out["decode"][f"{name}_m{m}"] = {"us": round(us, 2), "weight_gbs": round(gbs, 1)}
+            q, s = bf.quantize_cuda(x)
+            lin, lin_iqr = stats(lambda i: bf.linear(x, *ws[i]), copies, calls)
+            gem, gem_iqr = stats(lambda i: bf.gemm(q, s, *ws[i]), copies, calls)
+            wb = weight_bytes(n, k)
+            out["decode"][f"{name}_m{m}"] = {"us": round(lin, 2), "us_iqr": lin_iqr,
+                                             "weight_gbs": round(wb / (lin * 1e-6) / 1e9, 1),
+                                             "gemm_us": round(gem, 2), "gemm_us_iqr": gem_iqr,
+                                             "gemm_weight_gbs": round(wb / (gem * 1e-6) / 1e9, 1)}
         for m in PREFILL_M:
             x = make_x(m, k, seed=m).to(dev)
             q, s = bf.quantize_cuda(x)
             n_calls = max(copies, 8)
-            lin = timing.rotating_graph_us(lambda i: bf.linear(x, *ws[i]), copies, n_calls)
-            gem = timing.rotating_graph_us(lambda i: bf.gemm(q, s, *ws[i]), copies, n_calls)
+            lin, lin_iqr = stats(lambda i: bf.linear(x, *ws[i]), copies, n_calls)
+            gem, gem_iqr = stats(lambda i: bf.gemm(q, s, *ws[i]), copies, n_calls)
             f = fp8_gemm_flops(m, n, k)
-            out["prefill"][f"{name}_m{m}"] = {"linear_us": round(lin, 1), "gemm_us": round(gem, 1),
+            out["prefill"][f"{name}_m{m}"] = {"linear_us": round(lin, 1), "linear_us_iqr": lin_iqr,
+                                              "gemm_us": round(gem, 1), "gemm_us_iqr": gem_iqr,
                                               "linear_tflops": round(f / (lin * 1e-6) / 1e12, 1),
                                               "gemm_tflops": round(f / (gem * 1e-6) / 1e12, 1)}
             torch.cuda.empty_cache()
@@ -374,26 +389,22 @@ def sweeps(dev, calls=48):
     return out
 
 
-def run_probes(dev, gemm_tflops, sweeps_out):
+def run_probes(dev, gemm_tflops):
     """Same-session roofline probes on this GPU (libblockfp8_b200's
     bfp8_probe_*): the dense e4m3 tensor-core rate with no operand traffic,
-    and the HBM read rate; the headline GEMM and the decode sweep against
-    them.  The roofline object above keeps MEASURED_PEAKS.json's figures."""
+    and the HBM read rate; the headline GEMM against the first.  The
+    roofline object keeps MEASURED_PEAKS.json's figures beside them."""
     from blockfp8_b200 import _native
     tf, mpc = _native.probe_mma(256, 4000)
     buf = torch.empty(4 << 30, dtype=torch.uint8, device=dev)
     gbs = _native.probe_hbm_read(buf, reps=5)
     del buf
     torch.cuda.empty_cache()
-    out = {"fp8_mma_tflops": round(tf, 1), "fp8_mma_macs_per_clock_per_sm": round(mpc, 1),
-           "hbm_read_gbs": round(gbs, 1),
-           "headline_gemm_frac_of_mma_probe": round(gemm_tflops / tf, 4),
-           "how": "bfp8_probe_mma: 128x256x32 tcgen05 e4m3 MMAs back to back from shared memory on every "
-                  "SM; bfp8_probe_hbm_read: streaming 16-byte reads of a 4 GiB buffer"}
-    if sweeps_out:
-        dec = [v["weight_gbs"] for k_, v in sweeps_out["decode"].items() if int(k_.split("_m")[1]) <= 16]
-        out["decode_m_le_16_median_frac_of_read_probe"] = round(statistics.median(dec) / gbs, 4)
-    return out
+    return {"fp8_mma_tflops": round(tf, 1), "fp8_mma_macs_per_clock_per_sm": round(mpc, 1),
+            "hbm_read_gbs": round(gbs, 1),
+            "headline_gemm_frac_of_mma_probe": round(gemm_tflops / tf, 4),
+            "how": "bfp8_probe_mma: 128x256x32 tcgen05 e4m3 MMAs back to back from shared memory on every "
+                   "SM; bfp8_probe_hbm_read: streaming 16-byte reads of a 4 GiB buffer"}
 
 
 def profile_case(spec):
@@ -412,7 +423,8 @@ def profile_case(spec):
 
 
 # DRAM bytes (read + write) of one headline GEMM launch at N = 1, from one ncu
-# capture (profiles/gemm_kernel_gate_up_m8192_dram.md).
+# capture of that launch (the committed profile summary of the headline
+# GEMM); a recorded figure, not measured in this run.
 HEADLINE_TRAFFIC = 187.65e6 + 379.59e6
 
 
@@ -467,10 +479,12 @@ def main():
     # ---- kernel breakdown inside the same flushed protocol: quantizer, GEMM
     q, s = bf.quantize_cuda(x)
     quant_us, _ = time_device(lambda: bf.quantize_cuda(x), args.steps, flush)
-    gemm_med, gemm_us = time_device(lambda: bf.gemm(q, s, b, sb), args.steps, flush)
-    gemm_tflops = fp8_gemm_flops(m, n_per, k) / (gemm_us * 1e-6) / 1e12  # this rank's slice
+    quant_bytes = 3 * m * k + 4 * m * (-(-k // 128))  # bf16 in, e4m3 out, fp32 scales
+    gemm_med, gemm_mean = time_device(lambda: bf.gemm(q, s, b, sb), args.steps, flush)
+    gemm_tflops = fp8_gemm_flops(m, n_per, k) / (gemm_med * 1e-6) / 1e12  # this rank's slice, median launch
     pk = peaks()
     fp8_peak = 2.0 * pk["bf16_tflops"]
+    probes = run_probes(dev, gemm_tflops) if world == 1 else None
 
     # ---- e2e: host (pinned) activations in, host output back, through linear
     x_host = x_cpu.pin_memory()
@@ -501,15 +515,21 @@ def main():
             "roofline": {"bound": "tensor", "kernel": "gemm_kernel (tcgen05 e4m3)",
                          "achieved": round(gemm_tflops, 1), "peak": round(fp8_peak, 1),
                          "unit": "TFLOP/s", "frac": round(gemm_tflops / fp8_peak, 4),
+                         "frac_of_mma_probe": round(gemm_tflops / probes["fp8_mma_tflops"], 4) if probes else None,
                          "peak_source": f"2 x bf16_tflops of MEASURED_PEAKS.json ({pk['source']}): "
-                                        "dense e4m3 runs at twice the bf16 rate",
+                                        "dense e4m3 runs at twice the bf16 rate; frac_of_mma_probe divides by "
+                                        "this process's own back-to-back tcgen05 e4m3 MMA rate",
+                         "timing": "median GEMM launch over the timed steps, L2 flushed before each",
                          "traffic": HEADLINE_TRAFFIC if (world == 1 and (m, n_per, k) == (8192, 24576, 4096))
                          else None,
-                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one headline "
-                                           "launch (profiles/gemm_kernel_gate_up_m8192_dram.md); N = 1 only",
+                         "traffic_source": "dram__bytes_read.sum + dram__bytes_write.sum of one headline GEMM "
+                                           "launch from an ncu capture (a recorded figure, not this run); N = 1",
                          "algorithmic": f"2*M*N*K = {fp8_gemm_flops(m, n_per, k):.4g} FLOP per launch"},
-            "breakdown_us": {"quantize": round(quant_us, 2), "gemm_mean": round(gemm_us, 2),
+            "breakdown_us": {"quantize": round(quant_us, 2), "gemm_mean": round(gemm_mean, 2),
                              "gemm_median": round(gemm_med, 2), "linear_mean": round(mine * 1e3, 2)},
+            "quantizer": {"us": round(quant_us, 2), "gbs": round(quant_bytes / (quant_us * 1e-6) / 1e9, 1),
+                          "frac_of_hbm": round(quant_bytes / (quant_us * 1e-6) / 1e9 / pk["hbm_gbs"], 3),
+                          "bytes": quant_bytes, "timing": "median launch, L2 flushed before each"},
             "e2e": {"value": round(flops_total / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOPS",
                     "h2d_bytes_per_step": m * k * 2, "d2h_bytes_per_step": m * n_per * 2,
                     "ms_per_step": round(e2e_ms, 3)},
@@ -524,12 +544,18 @@ def main():
             line["decode_roofline"] = {
                 "bound": "hbm", "unit": "GB/s", "peak": pk["hbm_gbs"],
                 "peak_source": f"hbm_gbs of MEASURED_PEAKS.json ({pk['source']}, a copy figure)",
-                "timing": "linear (quantizer + GEMM), one CUDA graph of back-to-back calls over weight "
-                          "copies that together exceed L2 (cold weights), device time per call",
+                "timing": "linear (quantizer + GEMM; the weight-streaming kernel for M <= 32), one CUDA graph "
+                          "of back-to-back calls over weight copies that together exceed L2 (cold weights), "
+                          "median device time per call over the replays",
                 "min_frac_m_le_16": round(min(v["weight_gbs"] for v in best.values()) / pk["hbm_gbs"], 3),
                 "median_frac_m_le_16": round(statistics.median(v["weight_gbs"] for v in best.values())
-                                             / pk["hbm_gbs"], 3)}
-        line["probes"] = run_probes(dev, gemm_tflops, line.get("sweeps"))
+                                             / pk["hbm_gbs"], 3),
+                "gemm_median_frac_m_le_16": round(statistics.median(v["gemm_weight_gbs"] for v in best.values())
+                                                  / pk["hbm_gbs"], 3),
+                "us_m_le_16": {k_: v["us"] for k_, v in best.items()}}
+            probes["decode_m_le_16_median_frac_of_read_probe"] = round(
+                statistics.median(v["weight_gbs"] for v in best.values()) / probes["hbm_read_gbs"], 4)
+        line["probes"] = probes
         if not args.no_cpu:
             line["cpu_baseline"] = run_cpu_baseline()
     if rank == 0:

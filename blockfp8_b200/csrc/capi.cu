@@ -548,8 +548,10 @@ int launch_quant(const QuantParams& qp, cudaStream_t stream, int num_sms) {
   const int64_t tasks = int64_t(cdiv(qp.M, kQuantRows)) * cdiv(qp.kb, kQuantGroups);
   if (tasks == 0) return BFP8_OK;
   if (tasks >= (int64_t(1) << 31)) return fail(BFP8_EINVAL, "too many rows x K groups for one quantization launch");
-  // As many CTAs as are resident at once (four per SM at this register use).
-  const int grid = int(std::min<int64_t>(tasks, int64_t(num_sms) * 4));
+  // Eight CTAs per SM: more loads in flight per SM than the four that are
+  // resident at once, so the CTAs of the second wave start as the first ones
+  // drain (measured faster than one resident wave at M = 8192, K = 4096).
+  const int grid = int(std::min<int64_t>(tasks, int64_t(num_sms) * 8));
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kQuantThreads);
@@ -594,7 +596,7 @@ int static_scratch(int dev, unsigned char** out) {
 // two warps per CTA quantizing every K block of its range cost more than the
 // quantization kernel ahead of it (measured on B200), which it then uses.
 constexpr int kStreamMaxM = 32;
-constexpr int kStreamInGemmMaxM = 4;
+constexpr int kStreamInGemmMaxM = 2;
 
 bfp8_plan stream_plan(int M, int N, int K, int num_sms) {
   (void)N;
@@ -761,6 +763,7 @@ struct StreamLayout {
 };
 
 constexpr int kStreamPairSmem = 112 * 1024;
+constexpr int64_t kStreamDeepRingSpan = 16;  // K blocks per CTA from which the deep ring wins
 
 int stream_layout(int bn, bool quant, int M, const Derived& d, StreamLayout* out) {
   const int64_t span = (d.sk_work + d.sk_grid - 1) / d.sk_grid;
@@ -777,9 +780,14 @@ int stream_layout(int bn, bool quant, int M, const Derived& d, StreamLayout* out
     *o = {s, group, int(1024 + end), uint32_t(stage), uint32_t(off_sa), uint32_t(off_sb), uint32_t(off_bars)};
     return true;
   };
-  const int pair[][2] = {{3, 2}, {2, 2}, {3, 1}, {2, 1}};  // {stages, K blocks per stage}, two CTAs per SM
-  for (const auto& t : pair)
-    if (fits(t[0], t[1], kStreamPairSmem, out)) return BFP8_OK;
+  // A CTA whose range is long (many more K blocks than a 112 KB ring holds)
+  // streams for most of the call: it gains more from a deep ring of its own
+  // than from a second CTA of the next call beside it.
+  if (span < kStreamDeepRingSpan) {
+    const int pair[][2] = {{3, 2}, {2, 2}, {3, 1}, {2, 1}};  // {stages, K blocks per stage}, two CTAs per SM
+    for (const auto& t : pair)
+      if (fits(t[0], t[1], kStreamPairSmem, out)) return BFP8_OK;
+  }
   const int alone[][2] = {{3, 4}, {2, 4}, {4, 2}, {3, 2}, {2, 2}, {3, 1}, {2, 1}};
   for (const auto& t : alone)
     if (fits(t[0], t[1], kMaxSmem, out)) return BFP8_OK;
@@ -1069,7 +1077,11 @@ int bfp8_launch_gemm_noalloc(const bfp8_gemm_problem* p, bfp8_plan plan, void* s
   unsigned char* base = nullptr;
   if (int r = static_scratch(dev, &base)) return r;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // The array keeps the previous call's contents; counters must start at zero.
+  // The kernels leave every counter they use at zero, so after a normal call
+  // this clear changes nothing; it is here for the call after one whose
+  // bounded wait gave up (its counters were left mid-count), since the
+  // array outlives every call.  One small memset on the stream per split-K
+  // call, kept for that robustness.
   if (counters > 0) {
     e = cudaMemsetAsync(base, 0, size_t(counters) * 4, s);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(static scratch counters)");

@@ -153,12 +153,23 @@ class RowParallelGroup:
                 self.counters.append(ptrs[1])
                 self.outs.append(ptrs[2])
         self._group = group
+        self.broken = False
 
-    def linear(self, x: torch.Tensor, b_q: torch.Tensor, b_scales: torch.Tensor) -> torch.Tensor:
+    def linear(self, x: torch.Tensor, b_q: torch.Tensor, b_scales: torch.Tensor, check: bool = False) -> torch.Tensor:
         """sum over ranks of x_r @ W_r^T for this rank's x_r [M, K_r] (bf16) and
-        block-FP8 W_r [N, K_r]; [M, N] bf16, identical on every rank."""
+        block-FP8 W_r [N, K_r]; [M, N] bf16, identical on every rank.
+
+        check=True synchronises after the launch and raises RuntimeError if
+        a bounded wait of the kernel gave up (another rank stalled or never
+        launched): the output is then incomplete.  Once a wait has given up
+        the group's counters are inconsistent, so every later call raises
+        until the group is rebuilt (a check=False call cannot know; read
+        blockfp8_b200._native.device_status() to find out)."""
         from . import _native, capi
         from .layout import FP8_DTYPE
+
+        if self.broken:
+            raise RuntimeError("this row-parallel group saw a wait give up; close it and build a new one")
 
         if x.dtype != torch.bfloat16 or x.dim() != 2 or b_q.dtype != FP8_DTYPE or b_q.dim() != 2:
             raise ValueError("x must be 2-D bf16 and b_q 2-D float8_e4m3fn")
@@ -186,6 +197,12 @@ class RowParallelGroup:
         for qr in range(self.world):
             tp.partials[qr], tp.counters[qr], tp.out[qr] = self.partials[qr], self.counters[qr], self.outs[qr]
         capi.launch_gemm_tp(p, plan, tp, ws, cnt)
+        if check:
+            status = _native.device_status(reset=False)
+            if status:
+                self.broken = True
+                raise RuntimeError(f"a bounded wait of the row-parallel kernel gave up (status {status:#x}); "
+                                   "the output is incomplete and the group must be rebuilt")
         return out
 
     def close(self) -> None:

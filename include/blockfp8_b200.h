@@ -143,7 +143,9 @@ int bfp8_launch_gemm(const bfp8_gemm_problem* p, bfp8_plan plan, float* workspac
  * counters) is rejected with BFP8_EINVAL and nothing is launched.  The first
  * call on a device looks the array's address up (cudaGetSymbolAddress), so
  * make it before any stream capture.  Each call clears the counters it uses
- * (cudaMemsetAsync on the stream); every call shares the one array, so calls
+ * (cudaMemsetAsync on the stream; the kernels leave them zero, so this only
+ * matters after a call whose bounded wait gave up); every call shares the
+ * one array, so calls
  * that overlap on the GPU (other streams, other host threads) race and must
  * be serialised by the caller.  Allocates nothing.  Same results as
  * bfp8_launch_gemm under the same plan. */
