@@ -276,6 +276,17 @@ def reference_path():
     return quant, reference
 
 
+def arm_config(name, m, n, k, world):
+    """The workload both arms name (the reference arm times a row sample of
+    it on the host and says so in its cpu_baseline)."""
+    n_per = n // world
+    return {"workload": f"{name} linear (quantize + GEMM) M={m} N={n} K={k}, N "
+                        f"column-sharded into {world} slice(s) of {n_per}",
+            "M": m, "N": n, "K": k, "n_per_gpu": n_per,
+            "parallelism": f"column-parallel N/{world}, x replicated, no collective",
+            "l2": "flushed by a 512 MiB write before every timed step"}
+
+
 def run_reference(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -322,10 +333,10 @@ def run_reference(args):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "f64 (the reference's CPU path)", "data": "synthetic (seeded N(0,1) x, N(0,0.02) w)",
-        "config": {"workload": f"{name} linear M={m} N={n} K={k}, a sample of {rows} activation rows per "
-                               f"step (host CPU)", "M": m, "N": n, "K": k, "sample_rows": rows},
+        "config": arm_config(name, m, n, k, world),
         "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": cores, "kind": kind,
-                         "sample": f"{rows} of {m} rows per step: {what}"},
+                         "sample": f"{rows} of the {m} activation rows per step (host CPU, "
+                                   f"{cores} threads; TFLOPS counts the sample's 2*rows*N*K): {what}"},
         "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -507,11 +518,7 @@ def main():
             "dtype": "e4m3 x e4m3 -> f32 (bf16 in/out)",
             "data": "synthetic: seeded CPU N(0,1) bf16 activations, N(0,0.02) weights quantized in "
                     "128x128 blocks",
-            "config": {"workload": f"{name} linear (quantize + GEMM) M={m} N={n} K={k}, N "
-                                   f"column-sharded into {world} slice(s) of {n_per}",
-                       "M": m, "N": n, "K": k, "n_per_gpu": n_per,
-                       "parallelism": f"column-parallel N/{world}, x replicated, no collective",
-                       "l2": "flushed by a 512 MiB write before every timed step"},
+            "config": arm_config(name, m, n, k, world),
             "roofline": {"bound": "tensor", "kernel": "gemm_kernel (tcgen05 e4m3)",
                          "achieved": round(gemm_tflops, 1), "peak": round(fp8_peak, 1),
                          "unit": "TFLOP/s", "frac": round(gemm_tflops / fp8_peak, 4),
