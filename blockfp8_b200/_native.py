@@ -103,6 +103,7 @@ _SIGNATURES = {
     "bfp8_probe_block": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
     "bfp8_probe_quantizer": ([ctypes.c_float, ctypes.POINTER(ctypes.c_ulonglong), ctypes.POINTER(ctypes.c_ulonglong)],
                              ctypes.c_int),
+    "bfp8_probe_scale": ([ctypes.POINTER(ctypes.c_ulonglong), ctypes.POINTER(ctypes.c_ulonglong)], ctypes.c_int),
 }
 
 _capi = None
@@ -210,4 +211,12 @@ def probe_quantizer(eps: float = 1e-10) -> tuple[int, int]:
     the reference's division sequence over the whole bf16 input domain."""
     bad, first = ctypes.c_ulonglong(), ctypes.c_ulonglong()
     check(capi().bfp8_probe_quantizer(eps, ctypes.byref(bad), ctypes.byref(first)))
+    return bad.value, first.value
+
+
+def probe_scale() -> tuple[int, int]:
+    """(mismatching scales, first mismatch + 1) of the quantizer's amax / 448
+    against the IEEE division over every finite non-negative float."""
+    bad, first = ctypes.c_ulonglong(), ctypes.c_ulonglong()
+    check(capi().bfp8_probe_scale(ctypes.byref(bad), ctypes.byref(first)))
     return bad.value, first.value

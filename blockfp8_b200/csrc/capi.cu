@@ -1210,3 +1210,22 @@ extern "C" int bfp8_probe_quantizer(float eps, unsigned long long* mismatches, u
   if (first) *first = h[1];
   return BFP8_OK;
 }
+
+extern "C" int bfp8_probe_scale(unsigned long long* mismatches, unsigned long long* first) {
+  if (!mismatches) return bfp8::fail(BFP8_EINVAL, "probe arguments");
+  unsigned long long* d = nullptr;
+  cudaError_t err = cudaMalloc(&d, 2 * sizeof(unsigned long long));
+  if (err != cudaSuccess) return bfp8::cuda_fail(err, "cudaMalloc (probe)");
+  err = cudaMemset(d, 0, 2 * sizeof(unsigned long long));
+  if (err == cudaSuccess) {
+    bfp8::probe_scale_kernel<<<148 * 16, 256>>>(d);
+    err = cudaGetLastError();
+  }
+  unsigned long long h[2] = {0, 0};
+  if (err == cudaSuccess) err = cudaMemcpy(h, d, sizeof(h), cudaMemcpyDeviceToHost);
+  cudaFree(d);
+  if (err != cudaSuccess) return bfp8::cuda_fail(err, "probe launch");
+  *mismatches = h[0];
+  if (first) *first = h[1];
+  return BFP8_OK;
+}

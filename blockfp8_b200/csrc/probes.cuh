@@ -146,7 +146,7 @@ __global__ void __launch_bounds__(256) probe_read_kernel(const uint4* __restrict
 __global__ void __launch_bounds__(256) probe_quant_kernel(float eps, unsigned long long* out) {
   const uint32_t a = blockIdx.x;
   const float amax = fmaxf(eps, __uint_as_float(a << 16));
-  const float scale = amax / 448.f;
+  const float scale = amax / 448.f;  // the reference's division
   const float r = __frcp_rn(scale);
   unsigned long long bad = 0;
   for (uint32_t x0 = threadIdx.x * 8u; x0 < 65536u; x0 += blockDim.x * 8u) {
@@ -166,6 +166,23 @@ __global__ void __launch_bounds__(256) probe_quant_kernel(float eps, unsigned lo
         ++bad;
         atomicCAS(out + 1, 0ull, (static_cast<unsigned long long>(a) << 32) | (x + 1u));
       }
+    }
+  }
+  if (bad) atomicAdd(out, bad);
+}
+
+// scale_of (the quantizer's three-operation amax / 448) against the IEEE
+// division on every finite non-negative float: thread i of the grid checks
+// bit patterns i, i + stride, ... below 0x7F800000.  out[0] counts the
+// differences, out[1] holds the first as its bit pattern + 1.
+__global__ void __launch_bounds__(256) probe_scale_kernel(unsigned long long* out) {
+  unsigned long long bad = 0;
+  const uint32_t stride = gridDim.x * blockDim.x;
+  for (uint32_t b = blockIdx.x * blockDim.x + threadIdx.x; b < 0x7F800000u; b += stride) {
+    const float a = __uint_as_float(b);
+    if (__float_as_uint(scale_of(a)) != __float_as_uint(a / 448.f)) {
+      ++bad;
+      atomicCAS(out + 1, 0ull, static_cast<unsigned long long>(b) + 1ull);
     }
   }
   if (bad) atomicAdd(out, bad);

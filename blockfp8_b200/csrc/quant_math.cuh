@@ -13,15 +13,19 @@
 // - group_codes_fast: x / scale as x * r corrected once (Markstein, "Computation
 //   of elementary functions on the IBM RISC System/6000 processor", IBM J.
 //   Res. Dev. 34(1), 1990): r = RN(1 / scale), q = RN(x r),
-//   e = x - q scale (exact, one fma), q' = RN(q + e r) with x's sign on a
-//   zero; then the saturating conversion, which equals clamp-then-convert for
-//   finite quotients.  Three packed f32x2 operations per pair of values
-//   instead of two divisions.  The
-//   input domain is small -- x is bf16 and amax is eps or a bf16 magnitude --
-//   and tests/test_quant_fast_gpu.py compares the two paths on every (x,
-//   amax) pair of it, so the fast path is exact by exhaustion, not by
-//   argument.  Groups holding a NaN or an infinity take the exact path
-//   (their quotients are not finite).
+//   e = x - q scale (exact, one fma), q' = RN(q + e r); then the saturating
+//   conversion, which equals clamp-then-convert for finite quotients, and
+//   x's sign ORed into each code (it only changes x = -0, whose quotient
+//   the sequence returns as +0).  Three packed f32x2 operations per pair of
+//   values instead of two divisions.  The scale itself is amax / 448 by the
+//   same correction with the constant y = RN(1 / 448): q = RN(amax y),
+//   e = amax - 448 q, scale = RN(q + e y) -- three operations instead of a
+//   division (amax below 2^-100 divides).  The input domain is small -- x is bf16 and amax is eps or a
+//   bf16 magnitude -- and tests/test_quant_fast_gpu.py compares the fast
+//   codes with the division on every (x, amax) pair of it and the fast
+//   scale with the division on every finite non-negative float, so both are
+//   exact by exhaustion, not by argument.  Groups holding a NaN or an
+//   infinity take the exact path (their quotients are not finite).
 #pragma once
 
 #include <cuda_bf16.h>
@@ -56,14 +60,23 @@ __device__ __forceinline__ float group_scale(const float (&f)[8], float eps) {
 // The largest bf16 magnitude bit pattern of the group (|x| as a 16-bit
 // integer; the order of non-negative floats is the order of their bits), on
 // every lane of the half-warp; 0x7F80 or more means an infinity or NaN is in
-// the group.  All 32 lanes must call it.
+// the group.  All 32 lanes must call it (one warp reduction per half-warp).
 __device__ __forceinline__ uint32_t group_max_bits(const uint4& v) {
   const uint32_t m2 = __vmaxu2(__vmaxu2(v.x & 0x7FFF7FFFu, v.y & 0x7FFF7FFFu),
                                __vmaxu2(v.z & 0x7FFF7FFFu, v.w & 0x7FFF7FFFu));
-  uint32_t m = max(m2 & 0xFFFFu, m2 >> 16);
-#pragma unroll
-  for (int o = 8; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
-  return m;
+  return __reduce_max_sync(0xFFFFu << (threadIdx.x & 16u), max(m2 & 0xFFFFu, m2 >> 16));
+}
+
+// amax / 448, correctly rounded, for finite amax >= 0 (see the file comment).
+// Below 2^-100 the correction step can underflow (the quotient nears the
+// subnormal range), so there the division itself runs; eps keeps amax far
+// above that in practice.
+__device__ __forceinline__ float scale_of(float amax) {
+  constexpr float kInv448 = 1.f / 448.f;  // RN(1 / 448)
+  if (amax < 0x1p-100f) return amax / 448.f;
+  const float q = __fmul_rn(amax, kInv448);
+  const float e = __fmaf_rn(-q, 448.f, amax);
+  return __fmaf_rn(e, kInv448, q);
 }
 
 // The 8 e4m3 codes of a lane's values by the reference's sequence, packed
@@ -103,14 +116,15 @@ __device__ __forceinline__ uint2 group_codes_fast(const uint4& v, float scale, f
     const float2 x = make_float2(__uint_as_float(w[e] << 16), __uint_as_float(w[e] & 0xFFFF0000u));
     const float2 q = fma_x2(x, rr, nz);     // RN(x r)  (adding -0 leaves every product as it is)
     const float2 err = fma_x2(q, nss, x);   // x - q scale, exact
-    float2 qq = fma_x2(err, rr, q);         // RN(q + err r)
-    // x / scale has x's sign; only a zero quotient can lose it here (+0 plus
-    // -0 is +0), and -0 encodes as 0x80
-    qq.x = __uint_as_float(__float_as_uint(qq.x) | ((w[e] << 16) & 0x80000000u));
-    qq.y = __uint_as_float(__float_as_uint(qq.y) | (w[e] & 0x80000000u));
+    const float2 qq = fma_x2(err, rr, q);   // RN(q + err r)
     const uint32_t pair = __nv_cvt_float2_to_fp8x2(qq, __NV_SATFINITE, __NV_E4M3);
     packed[e >> 1] |= pair << (16 * (e & 1));
   }
+  // x / scale has x's sign and so has its code; the sequence only loses it
+  // for x = -0 (+0 plus -0 is +0).  The high byte of each bf16 carries its
+  // sign in bit 7, the bit of the e4m3 sign.
+  packed[0] |= __byte_perm(v.x, v.y, 0x7531) & 0x80808080u;
+  packed[1] |= __byte_perm(v.z, v.w, 0x7531) & 0x80808080u;
   return make_uint2(packed[0], packed[1]);
 }
 
@@ -126,7 +140,7 @@ __device__ __forceinline__ GroupQuant quantize_group(const uint4& v, float eps) 
   const uint32_t mbits = group_max_bits(v);
   if (mbits < 0x7F80u) {  // finite group (uniform across the half-warp)
     const float amax = fmaxf(eps, __uint_as_float(mbits << 16));
-    g.scale = amax / 448.f;
+    g.scale = scale_of(amax);
     g.codes = group_codes_fast(v, g.scale, __frcp_rn(g.scale));
   } else {  // an infinity or NaN: the reference's sequence as it stands
     float f[8];

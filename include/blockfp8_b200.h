@@ -259,6 +259,12 @@ int bfp8_probe_block(const void* a, const void* b, float* d, void* stream);
  * *mismatches = codes that differ; *first = (amax bits << 32) | (x bits + 1)
  * of the first one, 0 if none.  Synchronous; allocates a few bytes. */
 int bfp8_probe_quantizer(float eps, unsigned long long* mismatches, unsigned long long* first);
+/* Exhaustive check of the quantizer's scale: amax / 448 as the kernels form
+ * it (a product with RN(1/448) and one correction step) against the IEEE
+ * division, on every finite non-negative float amax.  *mismatches = scales
+ * that differ; *first = bits + 1 of the first one, 0 if none.  Synchronous;
+ * allocates a few bytes. */
+int bfp8_probe_scale(unsigned long long* mismatches, unsigned long long* first);
 
 #ifdef __cplusplus
 }
