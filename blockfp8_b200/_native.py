@@ -52,6 +52,32 @@ class QuantProblem(ctypes.Structure):
     ]
 
 
+class RmsNormQuantProblem(ctypes.Structure):
+    """bfp8_rmsnorm_quant_problem."""
+    _fields_ = [
+        ("x", ctypes.c_void_p), ("ldx", ctypes.c_int64),
+        ("residual", ctypes.c_void_p), ("ldr", ctypes.c_int64),
+        ("residual_out", ctypes.c_void_p), ("ldro", ctypes.c_int64),
+        ("weight", ctypes.c_void_p),
+        ("y", ctypes.c_void_p), ("ldy", ctypes.c_int64),
+        ("q", ctypes.c_void_p), ("ldq", ctypes.c_int64),
+        ("s", ctypes.c_void_p), ("s_m", ctypes.c_int64), ("s_k", ctypes.c_int64),
+        ("M", ctypes.c_int), ("H", ctypes.c_int),
+        ("variance_epsilon", ctypes.c_float), ("eps", ctypes.c_float),
+    ]
+
+
+class SiluMulQuantProblem(ctypes.Structure):
+    """bfp8_silu_mul_quant_problem."""
+    _fields_ = [
+        ("x", ctypes.c_void_p), ("ldx", ctypes.c_int64),
+        ("y", ctypes.c_void_p), ("ldy", ctypes.c_int64),
+        ("q", ctypes.c_void_p), ("ldq", ctypes.c_int64),
+        ("s", ctypes.c_void_p), ("s_m", ctypes.c_int64), ("s_k", ctypes.c_int64),
+        ("M", ctypes.c_int), ("I", ctypes.c_int), ("eps", ctypes.c_float),
+    ]
+
+
 TP_MAX_RANKS = 8
 IPC_HANDLE_BYTES = 64
 
@@ -95,6 +121,8 @@ _SIGNATURES = {
     "bfp8_tp_close": ([ctypes.c_void_p], ctypes.c_int),
     "bfp8_tp_free": ([ctypes.c_void_p], ctypes.c_int),
     "bfp8_launch_quantize": ([ctypes.POINTER(QuantProblem), ctypes.c_void_p], ctypes.c_int),
+    "bfp8_launch_rmsnorm_quant": ([ctypes.POINTER(RmsNormQuantProblem), ctypes.c_void_p], ctypes.c_int),
+    "bfp8_launch_silu_mul_quant": ([ctypes.POINTER(SiluMulQuantProblem), ctypes.c_void_p], ctypes.c_int),
     "bfp8_device_status": ([ctypes.c_int], ctypes.c_int64),
     "bfp8_probe_mma": ([ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_double),
                         ctypes.POINTER(ctypes.c_double)], ctypes.c_int),
@@ -168,6 +196,20 @@ def _register_fakes() -> None:
         m, k = x.shape
         q = x.new_empty((m, k), dtype=torch.float8_e4m3fn)
         s = x.new_empty(((k + 127) // 128, m), dtype=torch.float32).t()
+        return q, s
+
+    @torch.library.register_fake("blockfp8_b200::rms_norm_quant")
+    def _(x, weight, variance_epsilon, residual=None, eps=1e-10):
+        m, h = x.shape
+        q = x.new_empty((m, h), dtype=torch.float8_e4m3fn)
+        s = x.new_empty(((h + 127) // 128, m), dtype=torch.float32).t()
+        return q, s, (x.new_empty((m, h)) if residual is not None else x.new_empty((0,)))
+
+    @torch.library.register_fake("blockfp8_b200::silu_mul_quant")
+    def _(x, eps=1e-10):
+        m, i = x.shape[0], x.shape[1] // 2
+        q = x.new_empty((m, i), dtype=torch.float8_e4m3fn)
+        s = x.new_empty(((i + 127) // 128, m), dtype=torch.float32).t()
         return q, s
 
 

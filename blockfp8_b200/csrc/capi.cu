@@ -25,6 +25,7 @@
 
 #include "gemm_kernel.cuh"
 #include "probes.cuh"
+#include "producers.cuh"
 #include "quantize.cuh"
 #include "stream_gemm.cuh"
 
@@ -731,6 +732,75 @@ int bfp8_launch_quantize(const bfp8_quant_problem* qp, void* stream) {
   QuantParams q{static_cast<const __nv_bfloat16*>(p.x), p.ldx, static_cast<uint8_t*>(p.q), p.ldq,
                 p.s, p.s_m, p.s_k, p.M, p.K, cdiv(p.K, 128), p.eps};
   return launch_quant(q, static_cast<cudaStream_t>(stream), sms);
+}
+
+namespace bfp8 {
+namespace {
+
+// Shared checks of the producers' outputs: q (e4m3) and y (bf16) rows.
+int check_outputs(const void* q, int64_t ldq, const void* y, int64_t ldy, const float* s, int cols) {
+  if (!q && !y) return fail(BFP8_EINVAL, "nothing to write (q and y are both null)");
+  if (q && (!s || !aligned16(q) || ldq < cols || ldq % 16 != 0))
+    return fail(BFP8_EINVAL, "q must be row-major with 16-byte aligned rows, with scales");
+  if (y && (!aligned16(y) || ldy < cols || ldy % 8 != 0))
+    return fail(BFP8_EINVAL, "y must be row-major with 16-byte aligned rows");
+  return BFP8_OK;
+}
+
+int launch_with_pdl(const void* kernel, dim3 grid, void** args, cudaStream_t stream, const char* what) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kProdThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  set_pdl(cfg, attr);
+  cudaError_t e = cudaLaunchKernelExC(&cfg, kernel, args);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  return BFP8_OK;
+}
+
+}  // namespace
+}  // namespace bfp8
+
+int bfp8_launch_rmsnorm_quant(const bfp8_rmsnorm_quant_problem* pp, void* stream) {
+  if (!pp) return fail(BFP8_EINVAL, "null problem");
+  const bfp8_rmsnorm_quant_problem& p = *pp;
+  if (p.M < 0 || p.H <= 0 || p.H % 128 != 0 || p.H > kProdChunk * kProdMaxChunks)
+    return fail(BFP8_EINVAL, "H must be a positive multiple of 128, at most 16384");
+  if (p.M == 0) return BFP8_OK;
+  if (!p.x || !p.weight || !aligned16(p.x) || !aligned16(p.weight) || p.ldx < p.H || p.ldx % 8 != 0)
+    return fail(BFP8_EINVAL, "x and weight must be 16-byte aligned, x row-major");
+  if (p.residual && (!p.residual_out || !aligned16(p.residual) || !aligned16(p.residual_out) || p.ldr < p.H ||
+                     p.ldr % 8 != 0 || p.ldro < p.H || p.ldro % 8 != 0))
+    return fail(BFP8_EINVAL, "residual and residual_out must be row-major with 16-byte aligned rows");
+  if (int r = check_outputs(p.q, p.ldq, p.y, p.ldy, p.s, p.H)) return r;
+  if (!(p.eps > 0.f) || !(p.variance_epsilon >= 0.f)) return fail(BFP8_EINVAL, "eps must be positive");
+  RmsNormQuantParams k{static_cast<const __nv_bfloat16*>(p.x), p.ldx, static_cast<const __nv_bfloat16*>(p.residual),
+                       p.ldr, static_cast<__nv_bfloat16*>(p.residual_out), p.ldro,
+                       static_cast<const __nv_bfloat16*>(p.weight), static_cast<__nv_bfloat16*>(p.y), p.ldy,
+                       static_cast<uint8_t*>(p.q), p.ldq, p.s, p.s_m, p.s_k, p.M, p.H, p.variance_epsilon, p.eps};
+  void* args[] = {&k};
+  return launch_with_pdl(reinterpret_cast<const void*>(rmsnorm_quant_kernel), dim3(unsigned(p.M)), args,
+                         static_cast<cudaStream_t>(stream), "RMSNorm-quantize launch");
+}
+
+int bfp8_launch_silu_mul_quant(const bfp8_silu_mul_quant_problem* pp, void* stream) {
+  if (!pp) return fail(BFP8_EINVAL, "null problem");
+  const bfp8_silu_mul_quant_problem& p = *pp;
+  if (p.M < 0 || p.I <= 0 || p.I % 128 != 0) return fail(BFP8_EINVAL, "I must be a positive multiple of 128");
+  if (p.M == 0) return BFP8_OK;
+  if (p.M > 65535) return fail(BFP8_EINVAL, "at most 65535 rows per launch");
+  if (!p.x || !aligned16(p.x) || p.ldx < 2 * int64_t(p.I) || p.ldx % 8 != 0)
+    return fail(BFP8_EINVAL, "x must be row-major [M, 2I] with 16-byte aligned rows");
+  if (int r = check_outputs(p.q, p.ldq, p.y, p.ldy, p.s, p.I)) return r;
+  if (!(p.eps > 0.f)) return fail(BFP8_EINVAL, "eps must be positive");
+  SiluMulQuantParams k{static_cast<const __nv_bfloat16*>(p.x), p.ldx, static_cast<__nv_bfloat16*>(p.y), p.ldy,
+                       static_cast<uint8_t*>(p.q), p.ldq, p.s, p.s_m, p.s_k, p.M, p.I, p.eps};
+  void* args[] = {&k};
+  return launch_with_pdl(reinterpret_cast<const void*>(silu_mul_quant_kernel),
+                         dim3(unsigned(cdiv(p.I, kProdChunk)), unsigned(p.M)), args, static_cast<cudaStream_t>(stream),
+                         "SiLU-mul-quantize launch");
 }
 
 namespace bfp8 {

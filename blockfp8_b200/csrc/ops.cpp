@@ -255,7 +255,100 @@ std::string joined(int count, const char* (*name_of)(int)) {
 std::string config_names() { return joined(bfp8_num_configs(), bfp8_config_name); }
 std::string fused_config_names() { return joined(bfp8_num_fused_configs(), bfp8_fused_config_name); }
 
+// ---- producers that emit the linear's operand (torch.ops.blockfp8_b200) ---------
+// Not in the reference's extension: an RMSNorm and a SiLU-and-mul whose
+// outputs are the e4m3 codes and M-major scales blockfp8.gemm takes, so the
+// linear after them needs no quantization launch.
+
+std::tuple<at::Tensor, at::Tensor> quant_outputs(const at::Tensor& like, int64_t M, int64_t cols) {
+  at::Tensor q = at::empty({M, cols}, like.options().dtype(at::kFloat8_e4m3fn));
+  at::Tensor s = at::empty({cdiv(cols, 128), M}, like.options().dtype(at::kFloat)).t();
+  return {q, s};
+}
+
+// (q, scales, h): h = x + residual in bf16 when a residual is given (the
+// next layer's residual), else an empty tensor.
+std::tuple<at::Tensor, at::Tensor, at::Tensor> rms_norm_quant(const at::Tensor& x, const at::Tensor& weight,
+                                                              double variance_epsilon,
+                                                              const c10::optional<at::Tensor>& residual, double eps) {
+  const char* op = "blockfp8_b200.rms_norm_quant";
+  check_activations(x, op);
+  const int64_t M = x.size(0), H = x.size(1);
+  require(H % 128 == 0 && H <= 16384, op, "hidden size must be a multiple of 128, at most 16384");
+  require(weight.is_cuda() && weight.scalar_type() == at::kBFloat16 && weight.dim() == 1 && weight.size(0) == H &&
+              weight.stride(0) == 1 && aligned16(weight) && weight.device() == x.device(),
+          op, "weight must be a contiguous bfloat16 [H] tensor on x's device");
+  require(eps > 0 && variance_epsilon >= 0, op, "eps must be positive");
+  const at::cuda::CUDAGuard guard(x.device());
+  auto [q, s] = quant_outputs(x, M, H);
+  at::Tensor h;
+  bfp8_rmsnorm_quant_problem p{};
+  p.x = x.data_ptr();
+  p.ldx = x.stride(0);
+  if (residual.has_value()) {
+    const at::Tensor& r = *residual;
+    check_activations(r, op);
+    require(r.sizes() == x.sizes() && r.device() == x.device(), op, "residual must match x");
+    h = at::empty({M, H}, x.options());
+    p.residual = r.data_ptr();
+    p.ldr = r.stride(0);
+    p.residual_out = h.data_ptr();
+    p.ldro = h.stride(0);
+  } else {
+    h = at::empty({0}, x.options());
+  }
+  if (M == 0) return {q, s, h};
+  p.weight = weight.data_ptr();
+  p.q = q.data_ptr();
+  p.ldq = q.stride(0);
+  p.s = s.data_ptr<float>();
+  p.s_m = s.stride(0);
+  p.s_k = s.stride(1);
+  p.M = int(M);
+  p.H = int(H);
+  p.variance_epsilon = float(variance_epsilon);
+  p.eps = float(eps);
+  require_abi(bfp8_launch_rmsnorm_quant(&p, at::cuda::getCurrentCUDAStream().stream()));
+  return {q, s, h};
+}
+
+std::tuple<at::Tensor, at::Tensor> silu_mul_quant(const at::Tensor& x, double eps) {
+  const char* op = "blockfp8_b200.silu_mul_quant";
+  check_activations(x, op);
+  const int64_t M = x.size(0), I = x.size(1) / 2;
+  require(x.size(1) % 256 == 0, op, "x must be [M, 2I] with I a multiple of 128");
+  require(M <= 65535, op, "at most 65535 rows");
+  require(eps > 0, op, "eps must be positive");
+  const at::cuda::CUDAGuard guard(x.device());
+  auto [q, s] = quant_outputs(x, M, I);
+  if (M == 0) return {q, s};
+  bfp8_silu_mul_quant_problem p{};
+  p.x = x.data_ptr();
+  p.ldx = x.stride(0);
+  p.q = q.data_ptr();
+  p.ldq = q.stride(0);
+  p.s = s.data_ptr<float>();
+  p.s_m = s.stride(0);
+  p.s_k = s.stride(1);
+  p.M = int(M);
+  p.I = int(I);
+  p.eps = float(eps);
+  require_abi(bfp8_launch_silu_mul_quant(&p, at::cuda::getCurrentCUDAStream().stream()));
+  return {q, s};
+}
+
 }  // namespace
+
+TORCH_LIBRARY(blockfp8_b200, m) {
+  m.def("rms_norm_quant(Tensor x, Tensor weight, float variance_epsilon, Tensor? residual=None, "
+        "float eps=1e-10) -> (Tensor, Tensor, Tensor)");
+  m.def("silu_mul_quant(Tensor x, float eps=1e-10) -> (Tensor, Tensor)");
+}
+
+TORCH_LIBRARY_IMPL(blockfp8_b200, CUDA, m) {
+  m.impl("rms_norm_quant", &rms_norm_quant);
+  m.impl("silu_mul_quant", &silu_mul_quant);
+}
 
 TORCH_LIBRARY(blockfp8, m) {
   m.def("gemm(Tensor a, Tensor a_scales, Tensor b, Tensor b_scales, int config=-1, int split_k=0) -> Tensor");

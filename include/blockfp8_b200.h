@@ -226,6 +226,52 @@ int bfp8_set_weight_prefetch(int enabled);
  * (csrc/blockfp8.h:76).  Returns BFP8_OK, BFP8_EINVAL or BFP8_ECUDA. */
 int bfp8_launch_quantize(const bfp8_quant_problem* p, void* stream);
 
+/* The layers that feed a block-FP8 linear, emitting its e4m3 operand and
+ * M-major scales in the same kernel (no quantization launch between them and
+ * the GEMM).  No reference counterpart: the reference quantizes activations
+ * in a separate kernel (csrc/quant_sm89.cu) and notes fusing into the
+ * previous layer as outside its kernels (docs/design-tradeoffs.md:158-160).
+ * Codes and scales equal bfp8_launch_quantize applied to the bf16 output y,
+ * which the kernels also write when y is not null; q null = y only.
+ *
+ * RMSNorm: h = bf16(x + residual) (residual may be null; then h = x and
+ * residual_out is unused), y = bf16(bf16(h * rsqrt(mean(h^2) + variance_epsilon))
+ * * weight).  H a multiple of 128, at most 16384; rows 16-byte aligned. */
+typedef struct bfp8_rmsnorm_quant_problem {
+  const void* x;
+  int64_t ldx;
+  const void* residual;
+  int64_t ldr;
+  void* residual_out;
+  int64_t ldro;
+  const void* weight;
+  void* y;
+  int64_t ldy;
+  void* q;
+  int64_t ldq;
+  float* s;
+  int64_t s_m, s_k;
+  int M, H;
+  float variance_epsilon, eps;
+} bfp8_rmsnorm_quant_problem;
+int bfp8_launch_rmsnorm_quant(const bfp8_rmsnorm_quant_problem* p, void* stream);
+
+/* SiLU-and-mul: x [M, 2I] (gate then up), y = bf16(bf16(silu(gate)) * up) of
+ * shape [M, I].  I a multiple of 128; rows 16-byte aligned. */
+typedef struct bfp8_silu_mul_quant_problem {
+  const void* x;
+  int64_t ldx;
+  void* y;
+  int64_t ldy;
+  void* q;
+  int64_t ldq;
+  float* s;
+  int64_t s_m, s_k;
+  int M, I;
+  float eps;
+} bfp8_silu_mul_quant_problem;
+int bfp8_launch_silu_mul_quant(const bfp8_silu_mul_quant_problem* p, void* stream);
+
 /* The message of the last failed call on this host thread ("" if none).
  * No reference counterpart (the reference throws std::runtime_error). */
 const char* bfp8_last_error(void);
