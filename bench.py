@@ -361,7 +361,7 @@ def sweeps(dev, calls=48, replays=7):
     (timing.rotating_graph_stats)."""
     import blockfp8_b200 as bf
     from blockfp8_b200 import timing
-    out = {"decode": {}, "prefill": {}, "replays": replays,
+    out = {"decode": {}, "prefill": {}, "decode_producer": {}, "replays": replays,
            "timing": "per-call device time in one CUDA graph of back-to-back calls over weight copies that "
                      "together exceed L2 (cold weights); median [q1, q3] over the graph's replays"}
 
@@ -395,9 +395,42 @@ def sweeps(dev, calls=48, replays=7):
                                               "linear_tflops": round(f / (lin * 1e-6) / 1e12, 1),
                                               "gemm_tflops": round(f / (gem * 1e-6) / 1e12, 1)}
             torch.cuda.empty_cache()
+        if name in PRODUCER_OF:
+            out["decode_producer"].update(producer_sweep(bf, name, PRODUCER_OF[name], k, ws, copies, calls, stats))
         del ws, b0, sb0
         torch.cuda.empty_cache()
     return out
+
+
+# The layer in front of each linear of a decoder layer that has one on this
+# path: input / post-attention RMSNorm before qkv and gate_up, SiLU-and-mul
+# before down (o follows attention).
+PRODUCER_OF = {"qkv": "rms_norm", "gate_up": "rms_norm", "down": "silu_mul"}
+
+
+def producer_sweep(bf, name, kind, k, ws, copies, calls, stats):
+    """Decode M <= 16: the producer layer writing bf16 and then
+    blockfp8.linear, against the producer writing the e4m3 operand
+    (blockfp8_b200.producers) and then blockfp8.gemm; per-call device time."""
+    from blockfp8_b200 import producers
+    dev = ws[0][0].device
+    res = {}
+    w = (torch.rand(k, generator=torch.Generator().manual_seed(5)) + 0.5).to(torch.bfloat16).to(dev)
+    for m in [v for v in DECODE_M if v <= 16]:
+        if kind == "rms_norm":
+            x = make_x(m, k, seed=m).to(dev)
+            unfused = lambda i: bf.linear(producers.rms_norm(x, w, 1e-6), *ws[i])
+            fused = lambda i: bf.gemm(*producers.rms_norm_quant(x, w, 1e-6)[:2], *ws[i])
+        else:
+            x = make_x(m, 2 * k, seed=m).to(dev)
+            unfused = lambda i: bf.linear(producers.silu_mul(x), *ws[i])
+            fused = lambda i: bf.gemm(*producers.silu_mul_quant(x), *ws[i])
+        a, a_iqr = stats(unfused, copies, calls)
+        f, f_iqr = stats(fused, copies, calls)
+        res[f"{name}_m{m}"] = {"producer": kind, "bf16_then_linear_us": round(a, 2), "bf16_then_linear_iqr": a_iqr,
+                               "e4m3_then_gemm_us": round(f, 2), "e4m3_then_gemm_iqr": f_iqr,
+                               "saved_us": round(a - f, 2)}
+    return res
 
 
 def run_probes(dev, gemm_tflops):
@@ -436,7 +469,7 @@ def profile_case(spec):
 # DRAM bytes (read + write) of one headline GEMM launch at N = 1, from one ncu
 # capture of that launch (the committed profile summary of the headline
 # GEMM); a recorded figure, not measured in this run.
-HEADLINE_TRAFFIC = 187.65e6 + 379.59e6
+HEADLINE_TRAFFIC = 185.52e6 + 379.26e6
 
 
 def main():
