@@ -217,6 +217,14 @@ __device__ __forceinline__ unsigned long long atom_add_acq_rel_sys(unsigned long
   asm volatile("atom.acq_rel.sys.global.add.u64 %0, [%1], %2;" : "=l"(old) : "l"(ptr), "l"(v) : "memory");
   return old;
 }
+__device__ __forceinline__ void red_add_release_gpu(int* ptr, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_gpu(const int* ptr) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
+}
 __device__ __forceinline__ void red_add_release_sys(unsigned long long* ptr, unsigned long long v) {
   asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(ptr), "l"(v) : "memory");
 }

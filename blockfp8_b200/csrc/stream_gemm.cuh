@@ -11,9 +11,13 @@
 //   of W = tiles * k_tiles positions; CTA b of G takes positions
 //   [W b / G, W (b + 1) / G), so with G = the SM count every SM streams the
 //   same number of 16 KB weight tiles (+-1), whatever the layer's shape.  A
-//   tile cut between CTAs is summed by the last of its parts to arrive (a
-//   per-tile atomic counter), in K order from zero: deterministic, and no
-//   CTA ever waits for another.
+//   tile cut between CTAs is summed by the CTA holding its first part: the
+//   later parts lie at the starts of their CTAs' ranges, so they are done
+//   long before it reaches the tile at the end of its own range; each of
+//   them stores its fp32 sums and adds one (release) to the tile's counter,
+//   and the first part's CTA waits (bounded) for the count, then sums the
+//   parts in K order from zero, its own from registers: deterministic, and
+//   only a tile's owner ever waits, for parts that never wait.
 // - Stages: a ring stage holds up to `group` consecutive K blocks of one
 //   tile -- their weight tiles and their activation tiles -- requested
 //   together on one barrier.  A 128-row x 128-byte TMA box reads 128 pieces
@@ -106,6 +110,7 @@ enum StreamWaitSite : uint32_t {
   kSWaitAccFull = 21,
   kSWaitMmaDone = 22,
   kSWaitDrain = 23,
+  kSWaitParts = 24,  // the owner of a split tile waiting for the other parts
 };
 
 // Number of CTAs whose range starts at or before position x.
@@ -182,7 +187,6 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS) stream_kernel(c
   const uint32_t mma_done = s_bars + 8u * uint32_t(4 * S + 2 * ACC);
   uint32_t* misc = reinterpret_cast<uint32_t*>(smem + p.off_bars + 8u * uint32_t(4 * S + 2 * ACC + 1));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 1);
-  volatile int* last_flag = reinterpret_cast<volatile int*>(misc + 2);
   // QUANT: positions whose token scales are in sa_s (monotonic; the
   // epilogue may trail the quantizers by many stage uses, so it reads this
   // count rather than a stage barrier's phase).
@@ -464,30 +468,49 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS) stream_kernel(c
             for (int q = 0; q < BN; ++q)
               if (q < M) p.c[int64_t(q) * p.ldc + n] = __float2bfloat16_rn(accum[q]);
           }
-        } else {
-          // This part's sums: row `row`, tokens contiguous (16-byte pieces).
+        } else if (b != first) {
+          // A later part of the tile: its sums (row `row`, tokens contiguous,
+          // 16-byte pieces) to the workspace, then one release add on the
+          // tile's count; nothing waits here.
           float* ws = p.workspace + int64_t(g.tile) * p.max_pieces * (128 * MP) + row * MP;
-          const int64_t piece_stride = 128 * MP;
           if (row_ok) {
-            float4* w = reinterpret_cast<float4*>(ws + int64_t(b - first) * piece_stride);
+            float4* w = reinterpret_cast<float4*>(ws + int64_t(b - first) * (128 * MP));
 #pragma unroll
             for (int q = 0; q < BN; q += 4)
               if (q < M) __stcg(w + q / 4, make_float4(accum[q], accum[q + 1], accum[q + 2], accum[q + 3]));
           }
-          // Every thread's part is ordered before the count by the barrier
-          // and the gpu-scope release; the acquire makes the other parts
-          // visible to the last arriver.
+          // Every thread's stores are ordered before the add by the barrier
+          // and the add's gpu-scope release.
           named_bar_sync(1, 128);
-          if (et == 0) *last_flag = atom_add_acq_rel_gpu(p.counters + g.tile, 1) == pieces - 1;
+          if (et == 0) red_add_release_gpu(p.counters + g.tile, 1);
+        } else {
+          // The tile's first part, which this CTA reaches at the end of its
+          // range (the later parts lie at the starts of theirs): wait,
+          // bounded, for the other pieces - 1 parts, then sum the parts in K
+          // order from zero -- its own from registers -- and store.
+          float* ws = p.workspace + int64_t(g.tile) * p.max_pieces * (128 * MP) + row * MP;
+          const int64_t piece_stride = 128 * MP;
+          if (et == 0 && ok) {
+            const uint64_t w0 = globaltimer();
+            while (ld_acquire_gpu(p.counters + g.tile) < pieces - 1) {
+              if (*abort_flag || globaltimer() - w0 > kWaitTimeoutNs) {
+                if (!*abort_flag)
+                  record_status((0x5Bull << 56) | (uint64_t(kSWaitParts) << 32) | (uint64_t(blockIdx.x) << 8) | warp);
+                *abort_flag = 1;
+                break;
+              }
+              __nanosleep(32);
+            }
+          }
+          // (the acquire above, then the barrier: the other parts are visible to every thread)
           named_bar_sync(1, 128);
-          if (*last_flag) {
-            if (row_ok) {
-              // The parts in K order from zero (this CTA's own included),
-              // the loads of up to PB parts in flight at once.
+          {
+            if (row_ok && !*abort_flag) {
+              // the loads of up to PB parts in flight at once
               constexpr int PB = BN <= 16 ? 4 : 1;
 #pragma unroll
-              for (int q = 0; q < BN; ++q) accum[q] = 0.f;
-              for (int s0 = 0; s0 < pieces; s0 += PB) {
+              for (int q = 0; q < BN; ++q) accum[q] = 0.f + accum[q];  // part 0 added to zero
+              for (int s0 = 1; s0 < pieces; s0 += PB) {
                 float4 v[PB][BN / 4];
 #pragma unroll
                 for (int s = 0; s < PB; ++s) {
@@ -513,9 +536,9 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS) stream_kernel(c
               for (int q = 0; q < BN; ++q)
                 if (q < M) p.c[int64_t(q) * p.ldc + n] = __float2bfloat16_rn(accum[q]);
             }
-            if (et == 0) p.counters[g.tile] = 0;  // ready for the next launch
+            // every other part has arrived: ready for the next launch
+            if (et == 0 && !*abort_flag) p.counters[g.tile] = 0;
           }
-          named_bar_sync(1, 128);  // last_flag is rewritten by the next part
         }
 #pragma unroll
         for (int q = 0; q < BN; ++q) accum[q] = 0.f;
