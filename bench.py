@@ -244,6 +244,26 @@ def all_host_threads():
 
 
 def run_cpu_baseline(rows=REF_SAMPLE_ROWS, reps=2):
+    """The reference's own CPU path (the --impl reference arm, run in a
+    child process so that its `blockfp8` package does not replace this
+    process's), else the oracle port."""
+    if reference_path_exists():
+        env = dict(os.environ, RANK="0", WORLD_SIZE="1", LOCAL_RANK="0")
+        r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps",
+                            str(reps), "--warmup", "1"], env=env, capture_output=True, text=True, timeout=600)
+        lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+        if r.returncode == 0 and lines:
+            cb = json.loads(lines[-1])["cpu_baseline"]
+            if cb.get("kind") == "reference":
+                return cb
+    return run_port_baseline(rows, reps)
+
+
+def reference_path_exists():
+    return os.path.isdir(os.path.join(ROOT, "baseline", "_ref", "blockfp8"))
+
+
+def run_port_baseline(rows=REF_SAMPLE_ROWS, reps=2):
     O, xbits, b, sb, n, k = cpu_sample(rows)
     with all_host_threads():
         cpu_step(O, xbits, b, sb)  # warm (BLAS threads, page faults)
