@@ -264,6 +264,35 @@ def test_c_abi_rejects_bad_problems_without_launching():
     assert lib.bfp8_launch_quantize(ctypes.byref(q), None) == -1
 
 
+def test_producer_abi_rejects_bad_problems_without_launching():
+    lib = _native.capi()
+    fake = 1 << 20  # aligned non-null addresses: every check runs before any CUDA call
+    r = _native.RmsNormQuantProblem(x=fake, ldx=208, weight=fake, q=fake, ldq=208, s=fake, s_m=1, s_k=4,
+                                    M=4, H=208, variance_epsilon=1e-6, eps=1e-10)
+    assert lib.bfp8_launch_rmsnorm_quant(ctypes.byref(r), None) == -1
+    assert "multiple of 128" in lib.bfp8_last_error().decode()
+    r.H, r.ldx, r.ldq = 32768, 32768, 32768
+    assert lib.bfp8_launch_rmsnorm_quant(ctypes.byref(r), None) == -1
+    assert "at most 16384" in lib.bfp8_last_error().decode()
+    r.H, r.ldx, r.ldq, r.q, r.y = 256, 256, 256, None, None
+    assert lib.bfp8_launch_rmsnorm_quant(ctypes.byref(r), None) == -1
+    assert "nothing to write" in lib.bfp8_last_error().decode()
+    r.q, r.x = fake, fake + 8  # x not 16-byte aligned
+    assert lib.bfp8_launch_rmsnorm_quant(ctypes.byref(r), None) == -1
+    assert "16-byte aligned" in lib.bfp8_last_error().decode()
+    r.x, r.residual = fake, fake  # residual without residual_out
+    assert lib.bfp8_launch_rmsnorm_quant(ctypes.byref(r), None) == -1
+    assert "residual" in lib.bfp8_last_error().decode()
+    m = _native.SiluMulQuantProblem(x=fake, ldx=400, q=fake, ldq=200, s=fake, s_m=1, s_k=4, M=4, I=200, eps=1e-10)
+    assert lib.bfp8_launch_silu_mul_quant(ctypes.byref(m), None) == -1
+    assert "multiple of 128" in lib.bfp8_last_error().decode()
+    m.I, m.ldx, m.ldq = 256, 256, 256  # x must hold [gate | up] = 512 per row
+    assert lib.bfp8_launch_silu_mul_quant(ctypes.byref(m), None) == -1
+    assert "[M, 2I]" in lib.bfp8_last_error().decode()
+    m.M = 0  # an empty batch is a no-op
+    assert lib.bfp8_launch_silu_mul_quant(ctypes.byref(m), None) == 0
+
+
 def test_torch_op_schemas_are_the_reference_ones():
     schemas = {s.name: str(s) for s in torch._C._jit_get_all_schemas() if s.name.startswith("blockfp8::")}
     assert "blockfp8::gemm(Tensor a, Tensor a_scales, Tensor b, Tensor b_scales, int config=-1, " \
