@@ -592,12 +592,14 @@ int static_scratch(int dev, unsigned char** out) {
 
 // Decode batches (up to kStreamMaxM tokens) go to the weight-streaming
 // configurations: the smallest token tile that holds M, stream-K over every
-// SM.  The linear path quantizes inside that kernel up to
-// kStreamInGemmMaxM tokens (no quantization kernel between calls); beyond,
-// two warps per CTA quantizing every K block of its range cost more than the
-// quantization kernel ahead of it (measured on B200), which it then uses.
+// SM.  The linear path puts the quantization kernel ahead of it, which lets
+// the streaming kernel load its first weight stages while the quantizer
+// runs.  Quantizing inside the streaming kernel (plan.fused = 2, kept and
+// tested) is faster only when linears run back to back with nothing between
+// them, up to 2 tokens; with the other kernels of a model between the calls
+// it is 0.3-1.6 us slower per linear on B200, so the plan never picks it.
 constexpr int kStreamMaxM = 32;
-constexpr int kStreamInGemmMaxM = 2;
+constexpr int kStreamInGemmMaxM = 0;
 
 bfp8_plan stream_plan(int M, int N, int K, int num_sms) {
   (void)N;
