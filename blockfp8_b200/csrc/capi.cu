@@ -546,7 +546,9 @@ void set_pdl(cudaLaunchConfig_t& cfg, cudaLaunchAttribute* attr) {
 }
 
 int launch_quant(const QuantParams& qp, cudaStream_t stream, int num_sms) {
-  const int64_t tasks = int64_t(cdiv(qp.M, kQuantRows)) * cdiv(qp.kb, kQuantGroups);
+  // Four groups per task unless that leaves fewer tasks than two per SM.
+  const bool small = int64_t(cdiv(qp.M, kQuantRows)) * cdiv(qp.kb, kQuantGroups) < 2 * int64_t(num_sms);
+  const int64_t tasks = int64_t(cdiv(qp.M, kQuantRows)) * cdiv(qp.kb, small ? 1 : kQuantGroups);
   if (tasks == 0) return BFP8_OK;
   if (tasks >= (int64_t(1) << 31)) return fail(BFP8_EINVAL, "too many rows x K groups for one quantization launch");
   // Eight CTAs per SM: more loads in flight per SM than the four that are
@@ -559,7 +561,8 @@ int launch_quant(const QuantParams& qp, cudaStream_t stream, int num_sms) {
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   set_pdl(cfg, attr);
-  cudaLaunchKernelEx(&cfg, quantize_kernel, qp);
+  if (small) cudaLaunchKernelEx(&cfg, quantize_kernel<1>, qp);
+  else cudaLaunchKernelEx(&cfg, quantize_kernel<kQuantGroups>, qp);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "quantize kernel launch");
   return BFP8_OK;

@@ -36,9 +36,14 @@ struct QuantParams {
 
 constexpr int kQuantThreads = 256;
 constexpr int kQuantRows = kQuantThreads / 16;  // rows per CTA task
-constexpr int kQuantGroups = 4;                 // groups per half-warp task
+constexpr int kQuantGroups = 4;                 // groups per half-warp task (large batches)
 
+// G groups per half-warp task: 4 for large batches (more bytes in flight per
+// lane), 1 for decode-sized ones, whose few row blocks would otherwise leave
+// most SMs idle while each half-warp quantizes four groups one after another.
+template <int G>
 __global__ void __launch_bounds__(kQuantThreads) quantize_kernel(const QuantParams p) {
+  constexpr int kQuantGroups = G;
   // A GEMM launched behind this kernel with programmatic dependent launch may
   // start now: it only reads our output after griddepcontrol.wait.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -50,7 +55,7 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_kernel(const QuantPara
   const int row_blocks = (p.M + kQuantRows - 1) / kQuantRows;
   const int group_blocks = (p.kb + kQuantGroups - 1) / kQuantGroups;
   const int tasks = row_blocks * group_blocks;  // < 2^31 (checked by the host)
-  // Task t: rows rb * 16 .. + 15 (one per half-warp), groups gb * 4 .. + 3.
+  // Task t: rows rb * 16 .. + 15 (one per half-warp), groups gb * G .. + G - 1.
   // Row blocks vary fastest: neighbouring CTAs share a group range, so their
   // scale stores land in the same lines.  The loads of a CTA's next task go
   // out before the current one is converted.
