@@ -43,7 +43,6 @@ constexpr int kQuantGroups = 4;                 // groups per half-warp task (la
 // most SMs idle while each half-warp quantizes four groups one after another.
 template <int G>
 __global__ void __launch_bounds__(kQuantThreads) quantize_kernel(const QuantParams p) {
-  constexpr int kQuantGroups = G;
   // A GEMM launched behind this kernel with programmatic dependent launch may
   // start now: it only reads our output after griddepcontrol.wait.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -53,23 +52,23 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_kernel(const QuantPara
   const int lane16 = threadIdx.x & 15;
   const int half = threadIdx.x >> 4;  // 0 .. 15: the row within the task
   const int row_blocks = (p.M + kQuantRows - 1) / kQuantRows;
-  const int group_blocks = (p.kb + kQuantGroups - 1) / kQuantGroups;
+  const int group_blocks = (p.kb + G - 1) / G;
   const int tasks = row_blocks * group_blocks;  // < 2^31 (checked by the host)
   // Task t: rows rb * 16 .. + 15 (one per half-warp), groups gb * G .. + G - 1.
   // Row blocks vary fastest: neighbouring CTAs share a group range, so their
   // scale stores land in the same lines.  The loads of a CTA's next task go
   // out before the current one is converted.
-  auto load = [&](int t, uint4 (&v)[kQuantGroups]) {
+  auto load = [&](int t, uint4 (&v)[G]) {
     const int gb = t / row_blocks, rb = t - gb * row_blocks;
     const int row = rb * kQuantRows + half;
 #pragma unroll
-    for (int j = 0; j < kQuantGroups; ++j) {
-      const int col = (gb * kQuantGroups + j) * 128 + lane16 * 8;
+    for (int j = 0; j < G; ++j) {
+      const int col = (gb * G + j) * 128 + lane16 * 8;
       v[j] = make_uint4(0u, 0u, 0u, 0u);  // zeros leave the amax alone
       if (row < p.M && col < p.K) v[j] = __ldcs(reinterpret_cast<const uint4*>(p.x + int64_t(row) * p.ldx + col));
     }
   };
-  uint4 cur[kQuantGroups], nxt[kQuantGroups];
+  uint4 cur[G], nxt[G];
   int t = blockIdx.x;
   if (t < tasks) load(t, cur);
 #pragma unroll 1
@@ -80,15 +79,15 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_kernel(const QuantPara
     const bool row_ok = row < p.M;  // uniform per half-warp
     uint8_t* qrow = p.q + int64_t(row) * p.ldq;
 #pragma unroll
-    for (int j = 0; j < kQuantGroups; ++j) {
-      const int g = gb * kQuantGroups + j;
+    for (int j = 0; j < G; ++j) {
+      const int g = gb * G + j;
       const int col = g * 128 + lane16 * 8;
       const GroupQuant gq = quantize_group(cur[j], p.eps);  // all 32 lanes (shuffles)
       if (row_ok && col < p.K) *reinterpret_cast<uint2*>(qrow + col) = gq.codes;
       if (row_ok && g < p.kb && lane16 == 0) p.s[int64_t(row) * p.s_m + int64_t(g) * p.s_k] = gq.scale;
     }
 #pragma unroll
-    for (int j = 0; j < kQuantGroups; ++j) cur[j] = nxt[j];
+    for (int j = 0; j < G; ++j) cur[j] = nxt[j];
   }
 }
 
