@@ -18,12 +18,19 @@ torch.cuda.synchronize() on both sides of the K timed steps; nvidia-smi
 samples the clocks during them.
 
 At N = 1, rank 0 also reports:
-  decode   the four Qwen3-8B shapes x M in {1..32}, linear
-           time and weight GB/s = (N K + 4 nb kb) / t against HBM;
+  decode   the four Qwen3-8B shapes x M in {1..32}, linear and GEMM-only
+           time (median and interquartile range over graph replays) and
+           weight GB/s = (N K + 4 nb kb) / t against HBM;
+  decode_producer  RMSNorm / SiLU-and-mul writing bf16 then linear, against
+           the same layer writing the e4m3 operand then the GEMM alone;
   prefill  the four shapes x M in {100 .. 8192} (off-grid M included), linear
            and GEMM-only TFLOPS;
-  roofline of the dominant kernel (the GEMM) and cpu_baseline (the CPU
-           oracle on a row sample of the same workload, timed on this host).
+  quantizer  its own time, GB/s and fraction of the HBM copy peak;
+  roofline of the dominant kernel (the GEMM, median launch) with its
+           fraction of the measured peak and of this process's MMA probe,
+           and cpu_baseline (the reference's own CPU path on a row sample of
+           the same workload, timed on this host; the oracle port without
+           baseline/_ref).
 
 --impl reference times the reference's own CPU implementation of the path
 -- blockfp8.quant.quantize_activations + blockfp8.reference.reference_gemm,
