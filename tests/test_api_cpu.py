@@ -264,6 +264,22 @@ def test_c_abi_rejects_bad_problems_without_launching():
     assert lib.bfp8_launch_quantize(ctypes.byref(q), None) == -1
 
 
+def test_decode_linear_plans_quantize_ahead_of_the_streaming_kernel():
+    """Up to 32 tokens the plan is a weight-streaming configuration; the
+    fused (linear) plan puts the quantization kernel ahead of it at every M
+    (the streaming kernel prefetches weights while the quantizer runs)."""
+    lib = _native.capi()
+    names = [lib.bfp8_config_name(i).decode() for i in range(lib.bfp8_num_configs())]
+    for n, k in [(6144, 4096), (4096, 4096), (24576, 4096), (4096, 12288)]:
+        for m in [1, 2, 3, 4, 8, 16, 17, 32]:
+            plan = lib.bfp8_choose_plan(m, n, k, 148)
+            fplan = lib.bfp8_choose_fused_plan(m, n, k, 148)
+            assert names[plan.config].startswith("w128d") and plan.fused == 0
+            assert (fplan.config, fplan.splits, fplan.fused) == (plan.config, plan.splits, 1)
+            bn = int(names[plan.config][len("w128d"):])
+            assert bn >= m and (bn == 16 or bn // 2 < m)  # the smallest token tile that holds M
+
+
 def test_producer_abi_rejects_bad_problems_without_launching():
     lib = _native.capi()
     fake = 1 << 20  # aligned non-null addresses: every check runs before any CUDA call
