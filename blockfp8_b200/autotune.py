@@ -163,10 +163,10 @@ def write_fused_table(results, names) -> None:
         f.write("\n".join(lines) + "\n")
 
 
-def read_table(path=TABLE) -> dict:
-    """{(n, k, m): (config, splits)} of a generated plan_table.inc."""
+def read_table(path=None) -> dict:
+    """{(n, k, m): (config, splits)} of a generated plan_table.inc (TABLE by default)."""
     rows = {}
-    for line in open(path):
+    for line in open(path or TABLE):
         line = line.strip()
         if line.startswith("{") and line.endswith("},"):
             n, k, m, config, splits = (int(v) for v in line[1:-2].split(","))
@@ -176,7 +176,7 @@ def read_table(path=TABLE) -> dict:
 
 def write_table(results, names, merge=True) -> None:
     """Write the winners; with merge, rows of shapes not in `results` stay."""
-    rows = read_table() if merge and os.path.exists(TABLE) else {}
+    rows = read_table(TABLE) if merge and os.path.exists(TABLE) else {}
     for r in results:
         rows[(r["n"], r["k"], r["m"])] = (r["best"]["config"], r["best"]["splits"])
     order = {shape: i for i, shape in enumerate(list(LAYERS.values()) + list(tp_layers((2, 4, 8)).values()))}
